@@ -1,0 +1,254 @@
+/* pt_b200.h -- C ABI of libpt_b200.so, the B200 (sm_100a) implementation of the PrimeTTS v2.1
+ * MB-iSTFT decoder hot path.
+ *
+ * Part 1 is the drop-in boundary: every symbol the reference graph interpreter
+ * (runtime/v21/src/pt_v21_host.c) binds for its CUDA build, with the reference's names, argument
+ * meaning, return codes and threading rules (runtime/v21/src/pt_v21.h:208-259).  A build of the
+ * interpreter with -DPT_V21_CUDA links against this library instead of pt_v21_cuda.cu.
+ * Part 2 adds entry points the reference does not have (multi-GPU device selection, fused
+ * convT epilogue, the iSTFT+PQMF tail, and the batched device-resident decoder).
+ *
+ * All pointers are plain host or device pointers; sizes are element counts unless named *_bytes.
+ * Return codes: 0 = success, -1 = failure (a message is printed to stderr and kept for
+ * pt_b200_last_error()).  There is no CPU fallback: a context that was not initialised for the
+ * GPU makes every compute entry point fail with -1.
+ */
+#ifndef PT_B200_H_
+#define PT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PT_B200_API __attribute__((visibility("default")))
+#else
+#define PT_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------------------------------
+ * The interpreter's per-request context and tensor view.  The library reads and writes a handful
+ * of these fields (use_cuda, g_stream, g_arena*, conv_pad_in, conv_in_dev, conv_keep*,
+ * conv_out_dev, chain_mark, the counters), so the layout must be identical to the interpreter's
+ * struct (runtime/v21/src/pt_v21.h:79-162).  tests/test_abi.py checks every offset against the
+ * reference header.  When the reference header is already included, its definitions are used.
+ * ------------------------------------------------------------------------------------------- */
+#ifndef PT_V21_H_
+#define PT_B200_RANK 6
+typedef struct {
+  int dt;
+  int ndim;
+  int64_t d[PT_B200_RANK];
+  int64_t n;
+  void *p;
+  int dev;
+  int dev_res;
+  void *dev_p;
+  int alive;
+  void *base;
+  int view;
+} pt_tv;
+
+struct pt_ctx {
+  int use_cuda;                 /* 1 after pt_v21_cuda_init: conv/convT/matmul run on the GPU */
+  void *map;
+  size_t maplen;
+  char *base;
+  uint32_t n_tensor;
+  const char **cont_names;
+  float **cont_f32;
+  int *cont_isz;
+  int64_t *cont_n;
+  int *cont_ndim;
+  char *cont_path;
+  int *cont_shared;
+  int64_t *cont_dims;
+  int n_cont;
+  pt_tv *V;
+  float *wav;
+  int64_t wav_n;
+  int ck_n;
+  const int *ck_ids;
+  char ck_dir[512];
+  int dev_mode;
+  long n_conv, n_convT, n_matmul, n_alloc_fail;
+  double t_conv, t_convT, t_matmul, t_total;
+  double g_alloc_ms, g_copy_ms, g_kernel_ms, g_free_ms;
+  long g_calls;
+  int prof;
+  int prof_node_on;
+  long host_bytes_live, host_bytes_peak;
+  void *pool[64];
+  long pool_bytes, pool_cap;
+  long host_alloc_count;
+  double dev_bytes_weights, dev_bytes_arena, dev_bytes_stray;
+  double dev_bytes_res;
+  int devres_oom;
+  size_t arena_alloc_bytes;
+  char *skip;
+  int fuse;
+  int run_from, run_to;
+  int stream_inject_id;
+  pt_tv *stream_inject;
+  void *stream_seeds;
+  int stream_nseeds;
+  void *stream_state;
+  double *prof_node;
+  double t_ekind[96];
+  long n_ekind[96];
+  void *g_weights;              /* this library: its per-context state (device, arena, events) */
+  void *g_arena;                /* device arena base (bump allocator, mark/release) */
+  void *g_stream;               /* the context's own non-blocking cudaStream_t */
+  size_t g_arena_bytes, g_arena_used;
+  int64_t conv_pad_in;          /* >= 0: conv input rows are unpadded, the kernel pads by this */
+  const float *conv_in_dev;     /* chained conv input already on the device, or NULL */
+  int conv_keep;                /* 1: keep this conv's output on the device for the next conv */
+  int conv_keep_res;
+  int devadd_used;
+  int dev_live;
+  float *conv_out_dev;          /* set by pt_v21_conv when the output was kept */
+  void *chain_mark;             /* arena mark held while a conv chain is in flight */
+  void *devres;
+};
+typedef struct pt_ctx pt_ctx;
+#endif /* PT_V21_H_ */
+
+/* ============================================================================================
+ * Part 1 -- the reference's CUDA-layer symbols (runtime/v21/src/pt_v21.h:208-259)
+ * ========================================================================================== */
+
+/* Replaces pt_v21_cuda_prewarm (pt_v21.h:213; pt_v21_cuda.cu:719-751): creates the CUDA context
+ * of the selected device early.  The Nano clock ramp has no B200 counterpart. */
+PT_B200_API int pt_v21_cuda_prewarm(void);
+
+/* Replaces pt_v21_cuda_init (pt_v21.h:209; pt_v21_cuda.cu:753-798): binds the context to device
+ * $PT_V21_DEVICE (default 0), creates its non-blocking stream and device arena
+ * ($PT_V21_ARENA_MB MiB, default 64) and sets c->use_cuda = 1.  Weights become resident on first
+ * use and are shared by every context on the same device. */
+PT_B200_API int pt_v21_cuda_init(pt_ctx *c, int verbose);
+
+/* Replaces pt_v21_cuda_shutdown (pt_v21.h:214; pt_v21_cuda.cu:800-813). */
+PT_B200_API void pt_v21_cuda_shutdown(pt_ctx *c);
+
+/* Replaces pt_v21_conv (pt_v21.h:253-255; pt_v21_cuda.cu:1756-1957).
+ * Y[b][co][t] = bias[co] + sum_k sum_ci W[co][ci][k] X[b][ci][t*stride + k*dil - pad_in], then
+ * the fused epilogue codes epi0/epi1 (1 LeakyReLU a, 2 ReLU, 3 x*a, 4 x+a).
+ * X: host [batch][cin][ldx]; unpadded rows when c->conv_pad_in >= 0 (padding = conv_pad_in),
+ * zero-padded rows otherwise.  When c->conv_in_dev is set, X is ignored and that device buffer
+ * (a kept output of the previous conv) is read instead.  Y: host [batch][cout4][n] (padded rows,
+ * cout4 = round_up(cout, 4); every element written; ldy is unused, as in the reference).
+ * wp: packed weights [cout4/4][K][cin][4]; bias: [cout] or NULL.  wtab/btab >= 0 identify
+ * container records: the device copy is made once per device and reused by all contexts.
+ * c->conv_keep = 1 leaves the result on the device in c->conv_out_dev (Y untouched).
+ * Only stride 1 is supported (every conv of the v2.1 graph has stride 1). */
+PT_B200_API int pt_v21_conv(pt_ctx *c, const float *X, int64_t ldx, int64_t cin, float *Y, int64_t ldy,
+                int64_t n, int cout, int K, int stride, int pad, int dil, const float *wp,
+                const float *bias, int64_t batch, int wtab, int btab, int epi0, int epi1,
+                float a0, float a1);
+
+/* Replaces pt_v21_convT (pt_v21.h:257-259; pt_v21_cuda.cu:2351-2491): conv_transpose1d through
+ * the packed phase layout [s*cout4/4][ntap][cin][4], including the tail flush.
+ * X: host [batch][cin][ldx] (tin columns used); Y: host [batch][cout4][Lout],
+ * Lout = (tin-1)*s - 2*pad + K. */
+PT_B200_API int pt_v21_convT(pt_ctx *c, const float *X, int64_t ldx, int64_t cin, int64_t tin, float *Y,
+                 int64_t ldy, int cout, int s, int pad, int K, const float *wp, const float *bias,
+                 int64_t batch, int wtab, int btab);
+
+/* Replaces pt_v21_matmul (pt_v21.h:260-261; pt_v21_cuda.cu:2493-2636): C[m][nn] = A[m][k] B[k][nn]
+ * (row-major, leading dimensions lda/ldb/ldc), on the same tensor-core kernel. */
+PT_B200_API int pt_v21_matmul(pt_ctx *c, const float *A, int64_t m, int64_t k, int64_t lda, const float *B,
+                  int64_t ldb, int64_t nn, float *C, int64_t ldc);
+
+/* Replaces pt_v21_conv_pads_in_kernel (pt_v21.h:224; pt_v21_cuda.cu:457-463): always 1, the
+ * tensor-core conv pads with TMA out-of-bounds zero fill. */
+PT_B200_API int pt_v21_conv_pads_in_kernel(pt_ctx *c);
+
+/* Replace the device-residency helpers (pt_v21.h:229-247; pt_v21_cuda.cu:246-454): a residual
+ * Add (epi=1 fuses a LeakyReLU), a LeakyReLU, and their buffers.  Allocation helpers return NULL
+ * on failure so that the interpreter keeps the tensor on its host path. */
+PT_B200_API int pt_v21_devadd_run(pt_ctx *c, const float *a, const float *b, float *y, int64_t n, int epi,
+                      float alpha);
+PT_B200_API int pt_v21_devleaky_run(pt_ctx *c, const float *a, float *y, int64_t n, float alpha);
+PT_B200_API float *pt_v21_dev_upload(pt_ctx *c, const void *h, int64_t n);
+PT_B200_API void pt_v21_dev_sync_host(pt_ctx *c, void *host, const void *dev, int64_t n);
+PT_B200_API void *pt_v21_dev_alloc(pt_ctx *c, size_t bytes);
+PT_B200_API void pt_v21_dev_free(pt_ctx *c, void *p);
+PT_B200_API void pt_v21_dev_reclaim(pt_ctx *c);
+
+/* Replace the bookkeeping symbols (pt_v21.h:215-221). */
+PT_B200_API void pt_v21_cuda_active(int delta);
+PT_B200_API double pt_v21_cuda_weights_mib(pt_ctx *c);
+PT_B200_API int pt_v21_cuda_keepwarm(int iters);   /* no clock governor to ramp on B200: returns 0 */
+PT_B200_API long pt_v21_gpu_cur_freq(void);        /* -1: not readable without NVML (as in the reference) */
+PT_B200_API long pt_v21_gpu_max_freq(void);        /* max SM clock of the current device in Hz */
+
+/* ============================================================================================
+ * Part 2 -- extensions (no counterpart symbol in the reference)
+ * ========================================================================================== */
+
+/* pt_v21_cuda_init on an explicit device (request-parallel multi-GPU: one context per request
+ * thread, weights resident once per device). */
+PT_B200_API int pt_v21_cuda_init_dev(pt_ctx *c, int device, int verbose);
+
+/* pt_v21_convT with one fused epilogue op (codes as pt_v21_conv), e.g. the LeakyReLU that
+ * follows each upsampler in the graph (node /dec/resblocks.0/LeakyRelu). */
+PT_B200_API int pt_v21_convT_epi(pt_ctx *c, const float *X, int64_t ldx, int64_t cin, int64_t tin, float *Y,
+                     int64_t ldy, int cout, int s, int pad, int K, const float *wp,
+                     const float *bias, int64_t batch, int wtab, int btab, int epi0, float a0);
+
+/* The iSTFT + PQMF synthesis tail (graph nodes /dec/Reshape_6 ... /dec/Conv) for one request:
+ * post [72][Tp] (subband_conv_post output, host) -> wav [256*(Tp-1)/16] (host).
+ * pqmf: the [1][4][63] synthesis filter (ONNX layout, host). */
+PT_B200_API int pt_v21_istft_pqmf(pt_ctx *c, const float *post, int64_t Tp, const float *pqmf, float *wav);
+
+/* Decoder weights in the container's packed layouts (tools/export_v21.py:88-121): conv
+ * [cout4/4][K][cin][4], convT [4*cout4/4][4][cin][4], biases [cout]; pqmf [1][4][63].
+ * Resblock r (0..5): kernel (3,7,11)[r%3], convs1 dilations (1,3,5), convs2 dilation 1;
+ * r < 3 follow ups.0 (256 channels), r >= 3 follow ups.1 (128 channels). */
+typedef struct {
+  const float *pre_w, *pre_b;
+  const float *ups_w[2], *ups_b[2];
+  const float *rb_w1[6][3], *rb_b1[6][3];
+  const float *rb_w2[6][3], *rb_b2[6][3];
+  const float *post_w, *post_b;
+  const float *pqmf;
+} pt_b200_dec_weights;
+
+typedef struct pt_b200_decoder pt_b200_decoder;
+
+/* Uploads and re-lays-out the decoder weights on `device` (once; the handle is shareable by
+ * threads that serialise their calls).  NULL on failure. */
+PT_B200_API pt_b200_decoder *pt_b200_decoder_create(int device, const pt_b200_dec_weights *w);
+PT_B200_API void pt_b200_decoder_destroy(pt_b200_decoder *d);
+
+/* Decode a batch of independent requests in one device-resident pass (all requests share each
+ * layer's launches).  Request i has T[i] latent frames; z_host is the concatenation of the
+ * requests' [192][T[i]] latents, wav_host receives the concatenation of their [256*T[i]]
+ * waveforms.  Host buffers should be pinned for full copy speed.  stream: a cudaStream_t or NULL
+ * for the decoder's own stream.  Synchronous: returns after wav_host is written. */
+PT_B200_API int pt_b200_decode_batch(pt_b200_decoder *d, void *stream, int nreq, const int64_t *T,
+                         const float *z_host, float *wav_host);
+
+/* Same with device buffers (z_dev / wav_dev on the decoder's device, same concatenated layouts).
+ * Asynchronous on `stream`; the returned status covers argument and launch errors only --
+ * pt_b200_decoder_sync() waits and reports device-side errors. */
+PT_B200_API int pt_b200_decode_batch_device(pt_b200_decoder *d, void *stream, int nreq, const int64_t *T,
+                                const float *z_dev, float *wav_dev);
+PT_B200_API int pt_b200_decoder_sync(pt_b200_decoder *d, void *stream);
+
+/* One request, the reference's driver shape (an extension the survey lists as pt_v21_decode):
+ * z [192][T] host -> wav [256*T] host. */
+PT_B200_API int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav);
+
+/* Diagnostics: the last error message of the calling thread, and the number of this library's
+ * kernels launched by the calling thread since the last reset. */
+PT_B200_API const char *pt_b200_last_error(void);
+PT_B200_API long pt_b200_kernel_launches(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PT_B200_H_ */

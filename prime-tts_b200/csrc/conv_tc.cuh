@@ -1,0 +1,343 @@
+// conv_tc.cuh -- the implicit-GEMM Conv1d / ConvTranspose1d kernel on tcgen05 tensor cores.
+//
+// Problem (per batch item z): Y[m][n] = sum_{tap, ci} X[row(m, tap)][ci] * W[n][tap][ci]
+//   M = output time rows (128 per CTA tile, TMEM lanes), N = output channels (<= 256 per tile,
+//   TMEM columns), K = taps x input channels in 32-channel blocks (128-byte rows).
+//   row(m, tap) = m + row_off0 + tap * row_step:  conv -> row_off0 = -pad, row_step = dilation;
+//   convT phase decomposition -> rows are delay-line steps q, row_step = -1 (tap j reads q - j),
+//   and N = stride * cout4 covers every phase at once, so no zero-stuffed MACs are issued.
+//
+// Operands: activations channels-last [z][rows][cin32] and weights [n][tap][cin32], both fp32
+// values already rounded to tf32, TMA-loaded in 128-byte-swizzled K-major tiles.  Rows outside
+// the activation tensor are zero-filled by TMA, which is the convolution's zero padding (and the
+// convT head / tail flush).  The accumulator lives in TMEM; the epilogue warps read it back with
+// tcgen05.ld and apply bias, the fused elementwise ops and the stores.
+//
+// Warp roles (192 threads): warps 0-3 epilogue (TMEM lanes 32w..32w+31), warp 4 TMA producer,
+// warp 5 TMEM allocator + MMA issuer.  Every mbarrier wait is bounded (ptx.cuh).
+#pragma once
+#include <climits>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace ptb {
+
+constexpr int kBM = 128;       // rows per tile
+constexpr int kBK = 32;        // fp32 per k-block row (one 128 B swizzle row)
+constexpr int kThreads = 192;
+
+enum EpiMode : int {
+  EPI_PLAIN_CONV = 0,   // channel-major output [z][n][t] (the pt_v21_conv C-ABI layout)
+  EPI_PLAIN_CONVT = 1,  // channel-major convT output [z][co][oi], oi = q*s + r - pad
+  EPI_ROWS = 2,         // channels-last ragged rows (decoder conv)
+  EPI_ROWS_CONVT = 3,   // channels-last ragged rows (decoder upsampler)
+};
+
+struct ConvGeom {
+  int m_rows;     // output rows per batch item
+  int n_cols;     // N extent of the weight matrix (multiple of the N tile)
+  int cin32;      // activation row length = weight row length per tap
+  int ntap;
+  int row_off0;   // activation row of output row 0, tap 0
+  int row_step;   // activation row increment per tap
+  int nkb;        // ntap * cin32 / 32
+};
+
+struct EpiParams {
+  int mode;
+  const float *bias;       // [n_cols] zero-padded; may be null
+  // channel-major outputs
+  float *y;
+  long long ybatch, ldy;
+  int nstore;              // columns that are stored (cout4, or s * cout4 for convT)
+  int rowmajor;            // EPI_PLAIN_CONV only: store y[z][t][n] (matmul) instead of y[z][n][t]
+  long long tout;          // conv: rows stored; convT: output length Lout
+  int epi0, epi1;
+  float a0, a1;
+  int s, pad, cphase;      // convT: column n = r * cphase + co
+  long long q0;            // convT: delay-line step of tile row 0
+  // channels-last ragged outputs (decoder)
+  const unsigned char *mask;  // per output row: bit0 valid, bit1 duplicate into row - 2
+  const int *obase;           // convT: per input row g -> output row obase[g] + s*g + r
+  const float *res;           // residual input
+  const float *accin;         // branch-sum accumulator input
+  float *out0;                // fp32 output
+  float *out1;                // tf32-rounded leaky output (next conv's input)
+  int ldc, ldc1;
+  int acc_mode;               // 0 none, 2: v = accin + v, 3: v = (accin + v) / 3
+  float alpha1;
+};
+
+__device__ __forceinline__ float epi_op(float v, int op, float a) {
+  switch (op) {
+    case 1: return v >= 0.0f ? v : a * v;
+    case 2: return v > 0.0f ? v : 0.0f;
+    case 3: return v * a;
+    case 4: return v + a;
+    default: return v;
+  }
+}
+
+__device__ __forceinline__ float leaky(float v, float a) { return v >= 0.0f ? v : a * v; }
+
+template <int BN>
+struct TmemCols {
+  static constexpr uint32_t value = BN <= 32 ? 32u : BN <= 64 ? 64u : BN <= 128 ? 128u : 256u;
+};
+
+template <int BN, int STAGES>
+struct ConvSmem {
+  static constexpr int kA = kBM * kBK * 4;        // 16 KiB
+  static constexpr int kB = BN * kBK * 4;
+  static constexpr int kStage = kA + kB;
+  static constexpr int kBytes = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Epilogue for one 32-column chunk held by this thread (its TMEM lane = tile row).
+template <int BN>
+__device__ __forceinline__ void epilogue_chunk(const EpiParams &e, const float (&acc)[32], int z,
+                                               int row, int m_rows, int n_base) {
+  if (e.mode == EPI_PLAIN_CONV) {
+    if (row >= e.tout) return;
+    float *yz = e.y + (long long)z * e.ybatch + (e.rowmajor ? (long long)row * e.ldy : row);
+    const long long nstride = e.rowmajor ? 1 : e.ldy;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = n_base + i;
+      if (n < e.nstore) {
+        float v = acc[i] + (e.bias ? __ldg(e.bias + n) : 0.0f);
+        if (e.epi0) v = epi_op(v, e.epi0, e.a0);
+        if (e.epi1) v = epi_op(v, e.epi1, e.a1);
+        yz[(long long)n * nstride] = v;
+      }
+    }
+    return;
+  }
+  if (e.mode == EPI_PLAIN_CONVT) {
+    if (row >= m_rows) return;
+    const long long q = e.q0 + row;
+    float *yz = e.y + (long long)z * e.ybatch;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = n_base + i;
+      if (n < e.nstore) {
+        const int r = n / e.cphase, co = n - r * e.cphase;
+        const long long oi = q * e.s + r - e.pad;
+        if (oi >= 0 && oi < e.tout) {
+          float v = acc[i] + (e.bias ? __ldg(e.bias + n) : 0.0f);
+          if (e.epi0) v = epi_op(v, e.epi0, e.a0);
+          yz[(long long)co * e.ldy + oi] = v;
+        }
+      }
+    }
+    return;
+  }
+  // channels-last ragged rows
+  long long orow;
+  int col0;
+  if (e.mode == EPI_ROWS) {
+    if (row >= m_rows) return;
+    orow = row;
+    col0 = n_base;
+  } else {
+    if (row >= m_rows) return;
+    const int base = __ldg(e.obase + row);
+    if (base == INT_MIN) return;
+    const int r = n_base / e.cphase;
+    orow = (long long)base + (long long)e.s * row + r;
+    col0 = n_base - r * e.cphase;
+  }
+  const unsigned char mk = __ldg(e.mask + orow);
+  if (!(mk & 1)) return;
+  // columns of this chunk that exist in the output rows (conv_post: 80-wide tile, 72 real);
+  // nstore counts columns of one output row (one phase for the upsampler)
+  const int lim = e.nstore - col0 < 32 ? e.nstore - col0 : 32;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const float4 b = (e.bias && i < lim) ? __ldg(reinterpret_cast<const float4 *>(e.bias + n_base + i))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[i + 0] = acc[i + 0] + b.x;
+    v[i + 1] = acc[i + 1] + b.y;
+    v[i + 2] = acc[i + 2] + b.z;
+    v[i + 3] = acc[i + 3] + b.w;
+  }
+  const long long off = orow * e.ldc + col0;
+  if (e.res) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      if (i >= lim) break;
+      const float4 r4 = *reinterpret_cast<const float4 *>(e.res + off + i);
+      v[i + 0] += r4.x;
+      v[i + 1] += r4.y;
+      v[i + 2] += r4.z;
+      v[i + 3] += r4.w;
+    }
+  }
+  if (e.acc_mode) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      if (i >= lim) break;
+      const float4 a4 = *reinterpret_cast<const float4 *>(e.accin + off + i);
+      if (e.acc_mode == 2) {
+        v[i + 0] = a4.x + v[i + 0];
+        v[i + 1] = a4.y + v[i + 1];
+        v[i + 2] = a4.z + v[i + 2];
+        v[i + 3] = a4.w + v[i + 3];
+      } else {
+        v[i + 0] = (a4.x + v[i + 0]) / 3.0f;
+        v[i + 1] = (a4.y + v[i + 1]) / 3.0f;
+        v[i + 2] = (a4.z + v[i + 2]) / 3.0f;
+        v[i + 3] = (a4.w + v[i + 3]) / 3.0f;
+      }
+    }
+  }
+  if (e.out0) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      if (i >= lim) break;
+      *reinterpret_cast<float4 *>(e.out0 + off + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+  }
+  if (e.out1) {
+    const long long off1 = orow * e.ldc1 + col0;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      if (i >= lim) break;
+      const float4 w = make_float4(tf32_rna(leaky(v[i], e.alpha1)), tf32_rna(leaky(v[i + 1], e.alpha1)),
+                                   tf32_rna(leaky(v[i + 2], e.alpha1)), tf32_rna(leaky(v[i + 3], e.alpha1)));
+      *reinterpret_cast<float4 *>(e.out1 + off1 + i) = w;
+      if (mk & 2) *reinterpret_cast<float4 *>(e.out1 + off1 - 2LL * e.ldc1 + i) = w;
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const ConvGeom g, const EpiParams e, uint32_t *gerr) {
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tcgen05 M=128 needs N % 16 == 0, <= 256");
+  using S = ConvSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;            // 1024 B: swizzle-atom aligned
+  uint8_t *gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + STAGES * S::kStage;         // full[S], empty[S], acc, drain
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  const uint32_t accbar = bar0 + 8u * (2 * STAGES);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + STAGES * S::kStage + 8 * (2 * STAGES + 2));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN, z = blockIdx.z;
+  constexpr uint32_t kCols = TmemCols<BN>::value;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(accbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const int kc = g.cin32 / kBK;
+      int issued[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+      bool ok = true;
+      for (int kb = 0; kb < g.nkb && ok; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t par = ((kb / STAGES) & 1) ^ 1;
+        if (!mbar_wait(empty(s), par, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        const int tap = kb / kc, c = kb - tap * kc;
+        const uint32_t sa = base + s * S::kStage, sb = sa + S::kA;
+        mbar_expect_tx(full(s), S::kStage);
+        tma_load_3d(sa, &tmA, full(s), c * kBK, m0 + g.row_off0 + tap * g.row_step, z);
+        tma_load_2d(sb, &tmB, full(s), tap * g.cin32 + c * kBK, n0);
+        ++issued[s];
+      }
+      if (!ok) {
+        // drain: every issued load must land before this CTA's shared memory is released
+        for (int s = 0; s < STAGES; ++s) {
+          if (!issued[s]) continue;
+          const uint32_t par = (issued[s] - 1) & 1;
+          uint32_t it = 0;
+          while (!mbar_try_wait(full(s), par) && ++it < kWaitLimit) {
+          }
+          if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = idesc_tf32(kBM, BN);
+      bool ok = true;
+      for (int kb = 0; kb < g.nkb; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(full(s), (kb / STAGES) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = base + s * S::kStage, sb = sa + S::kA;
+        const uint64_t da = sdesc_kmajor_sw128(sa), db = sdesc_kmajor_sw128(sb);
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k)  // K = 8 tf32 (32 bytes) per instruction
+          mma_tf32(tmem, da + 2u * k, db + 2u * k, idesc, (kb | k) != 0);
+        mma_commit(empty(s));  // frees the stage once these MMAs have read it
+      }
+      mma_commit(accbar);
+      if (!ok) {
+        // MMAs already issued must finish before TMEM is released
+        uint32_t it = 0;
+        while (!mbar_try_wait(accbar, 0) && ++it < kWaitLimit) {
+        }
+        if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 0..3
+    if (mbar_wait(accbar, 0, abort_flag, gerr, ERR_WAIT_ACC)) {
+      tc_fence_after();
+      const int row = m0 + warp * 32 + lane;
+      const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+      for (int j = 0; j < (BN + 31) / 32; ++j) {
+        float acc[32];
+        tmem_ld32(tl + 32u * j, acc);
+        epilogue_chunk<BN>(e, acc, z, row, g.m_rows, n0 + 32 * j);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+}  // namespace ptb

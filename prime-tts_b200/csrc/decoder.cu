@@ -1,0 +1,513 @@
+// decoder.cu -- the whole MB-iSTFT decoder device-resident, for a batch of independent requests.
+//
+// Ragged batch layout.  At each time resolution (level 0: latent frames T, level 1: 4T after
+// ups.0, level 2: 16T after ups.1) the requests are stacked along time in one channels-last
+// tensor [rows][C], each request's rows preceded and followed by kGap zero rows.  kGap (32)
+// exceeds every conv's reach (dilation 5 x (11-1)/2 = 25 rows), so one launch per layer computes
+// every request exactly as if it ran alone: the zero gap rows are the convolutions' zero padding,
+// and the epilogue never writes them (a per-row mask), so they stay zero.
+//
+// Graph wiring (ref/v21_graph_trace.txt 3819-4065), with every elementwise node fused:
+//   conv_pre(+LeakyRelu) -> ups.0 (writes u and leaky(u)) ->
+//   per resblock r, stage j: convs1 (+LeakyRelu) -> convs2 (+ residual add, + leaky for the next
+//   stage; the last stage of the last resblock also does /dec/Add, /dec/Add_1, /3, LeakyRelu) ->
+//   ups.1 -> the same MRF at 128 channels (final LeakyRelu 0.01 and the (1,0) reflection pad row)
+//   -> subband_conv_post -> the iSTFT/PQMF tail kernel.
+#include <climits>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/pt_b200.h"
+#include "common.cuh"
+
+namespace ptb {
+int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
+                  const long long *wav0, int nreq, long long max_tp, const float *pqmf_dev,
+                  float *wav_dev, cudaStream_t st);
+}  // namespace ptb
+
+using namespace ptb;
+
+namespace {
+
+constexpr int kGap = 32;
+constexpr int kK[3] = {3, 7, 11};
+constexpr int kD[3] = {1, 3, 5};
+constexpr float kLr = 0.10000000149011612f;
+constexpr float kLrFinal = 0.009999999776482582f;
+
+struct DLayer {
+  float *w = nullptr, *b = nullptr;  // [n_pad][ntap][cin32] tf32, bias [round_up(n_pad, 32)]
+  int n_pad = 0, bn = 0, cin32 = 0, ntap = 0;
+};
+
+// Stage packed weights into the kernel layout on the device (once per decoder).
+int make_layer(DLayer *L, const float *wp, const float *bias, int rows4, int ntap, int cin,
+               int cout, int cphase, cudaStream_t st) {
+  L->ntap = ntap;
+  L->cin32 = (int)round_up(cin, kBK);
+  if (pick_bn(rows4, &L->bn, &L->n_pad)) return -1;
+  const size_t pbytes = (size_t)rows4 * ntap * cin * 4;
+  float *dp = nullptr;
+  PTB_CUDA(cudaMalloc(&L->w, (size_t)L->n_pad * ntap * L->cin32 * 4));
+  PTB_CUDA(cudaMalloc(&L->b, (size_t)round_up(L->n_pad, 32) * 4));
+  PTB_CUDA(cudaMalloc(&dp, pbytes));
+  PTB_CUDA(cudaMemcpyAsync(dp, wp, pbytes, cudaMemcpyHostToDevice, st));
+  if (stage_packed_w(dp, rows4, ntap, cin, L->w, L->n_pad, L->cin32, st)) return -1;
+  std::vector<float> hb((size_t)round_up(L->n_pad, 32), 0.0f);
+  for (int n = 0; n < rows4; ++n)
+    if (n % cphase < cout) hb[n] = bias[n % cphase];
+  PTB_CUDA(cudaMemcpyAsync(L->b, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice, st));
+  PTB_CUDA(cudaStreamSynchronize(st));
+  cudaFree(dp);
+  return 0;
+}
+
+// scatter the concatenated channel-major latents [192][T_i] into the level-0 rows, tf32-rounded
+__global__ void stage_z_kernel(const float *__restrict__ z, const long long *__restrict__ zoff,
+                               const long long *__restrict__ T, const long long *__restrict__ a0,
+                               float *__restrict__ Z) {
+  __shared__ float tile[32][33];
+  const int r = blockIdx.z;
+  const long long Tr = T[r];
+  const long long t0 = (long long)blockIdx.x * 32;
+  if (t0 >= Tr) return;
+  const int c0 = blockIdx.y * 32;
+  const float *zr = z + zoff[r];
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long t = t0 + threadIdx.x;
+    tile[i][threadIdx.x] = t < Tr ? zr[(long long)(c0 + i) * Tr + t] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long t = t0 + i;
+    if (t < Tr) Z[(a0[r] + t) * 192 + c0 + threadIdx.x] = tf32_rna(tile[threadIdx.x][i]);
+  }
+}
+
+struct Plan {
+  std::vector<int64_t> T;
+  int64_t R[3] = {0, 0, 0};
+  int64_t max_T = 0, total_z = 0, total_wav = 0;
+  // device tables
+  unsigned char *mask[3] = {nullptr, nullptr, nullptr};
+  unsigned char *mask_refl = nullptr, *mask_post = nullptr;
+  int *ob01 = nullptr, *ob12 = nullptr;
+  long long *zoff = nullptr, *Td = nullptr, *a0 = nullptr;
+  long long *row0 = nullptr, *tp = nullptr, *wav0 = nullptr;
+  void *table_block = nullptr;
+  size_t table_bytes = 0;
+};
+
+}  // namespace
+
+struct pt_b200_decoder {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t *gerr = nullptr, *gerr_host = nullptr;
+  DLayer pre, ups[2], rb1[6][3], rb2[6][3], post;
+  float *pqmf = nullptr;
+  std::mutex mu;
+  Plan plan;
+  bool have_plan = false;
+  // activation buffers (grown on demand, zeroed when the plan changes)
+  void *act = nullptr;
+  size_t act_bytes = 0;
+  float *Z = nullptr, *X0 = nullptr;
+  float *U[2], *LU[2], *XB[2], *XT[2], *H[2], *ACC[2], *OUT1 = nullptr, *P = nullptr, *POST = nullptr;
+  float *zbuf = nullptr, *wavbuf = nullptr;  // staging for the host-buffer entry point
+  size_t zbuf_bytes = 0, wavbuf_bytes = 0;
+};
+
+namespace {
+
+int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
+  Plan &p = d->plan;
+  if (d->have_plan && (int)p.T.size() == nreq && std::memcmp(p.T.data(), T, sizeof(int64_t) * nreq) == 0)
+    return 0;
+  if (p.table_block) cudaFree(p.table_block);
+  d->have_plan = false;
+  p = Plan();
+  p.T.assign(T, T + nreq);
+  const int64_t scale[3] = {1, 4, 16};
+  std::vector<int64_t> a[3];
+  for (int l = 0; l < 3; ++l) {
+    int64_t off = kGap;
+    for (int i = 0; i < nreq; ++i) {
+      a[l].push_back(off);
+      off += scale[l] * T[i] + kGap;
+    }
+    p.R[l] = off;
+  }
+  for (int i = 0; i < nreq; ++i) {
+    PTB_REQUIRE(T[i] >= 2, "pt_b200: request %d has %lld frames (need >= 2)", i, (long long)T[i]);
+    p.max_T = T[i] > p.max_T ? T[i] : p.max_T;
+    p.total_z += 192 * T[i];
+    p.total_wav += 256 * T[i];
+  }
+  PTB_REQUIRE(p.R[2] < (int64_t)INT_MAX / 2, "pt_b200: batch too large (%lld level-2 rows)",
+              (long long)p.R[2]);
+  // host tables in one pinned block
+  std::vector<unsigned char> m[3], mr, mp;
+  for (int l = 0; l < 3; ++l) m[l].assign((size_t)p.R[l], 0);
+  for (int l = 0; l < 3; ++l)
+    for (int i = 0; i < nreq; ++i)
+      std::memset(m[l].data() + a[l][i], 1, (size_t)(scale[l] * T[i]));
+  mr = m[2];
+  mp.assign((size_t)p.R[2], 0);
+  for (int i = 0; i < nreq; ++i) {
+    mr[(size_t)a[2][i] + 1] |= 2;  // local row 1 is mirrored into row -1 (reflection pad (1,0))
+    std::memset(mp.data() + a[2][i] - 1, 1, (size_t)(16 * T[i] + 1));
+  }
+  std::vector<int> ob01((size_t)p.R[0], INT_MIN), ob12((size_t)p.R[1], INT_MIN);
+  for (int i = 0; i < nreq; ++i) {
+    // delay-line steps q = 1 .. T+1 of request i produce its outputs o = 4q + r - 6
+    for (int64_t q = 1; q <= T[i] + 1; ++q) {
+      ob01[(size_t)(a[0][i] + q)] = (int)(a[1][i] - 4 * a[0][i] - 6);
+    }
+    for (int64_t q = 1; q <= 4 * T[i] + 1; ++q) {
+      ob12[(size_t)(a[1][i] + q)] = (int)(a[2][i] - 4 * a[1][i] - 6);
+    }
+  }
+  std::vector<long long> zoff(nreq), Td(nreq), a0(nreq), row0(nreq), tp(nreq), wav0(nreq);
+  long long zo = 0, wo = 0;
+  for (int i = 0; i < nreq; ++i) {
+    zoff[i] = zo;
+    Td[i] = T[i];
+    a0[i] = a[0][i];
+    row0[i] = a[2][i] - 1;
+    tp[i] = 16 * T[i] + 1;
+    wav0[i] = wo;
+    zo += 192 * T[i];
+    wo += 256 * T[i];
+  }
+  // one device block: masks, convT row maps, per-request tables
+  auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  size_t off[12], tot = 0;
+  const size_t sz[12] = {(size_t)p.R[0], (size_t)p.R[1], (size_t)p.R[2], (size_t)p.R[2],
+                         (size_t)p.R[2], ob01.size() * 4, ob12.size() * 4, (size_t)nreq * 8,
+                         (size_t)nreq * 8, (size_t)nreq * 8, (size_t)nreq * 8, (size_t)nreq * 24};
+  for (int k = 0; k < 12; ++k) {
+    off[k] = tot;
+    tot += al(sz[k]);
+  }
+  PTB_CUDA(cudaMalloc(&p.table_block, tot));
+  char *base = static_cast<char *>(p.table_block);
+  std::vector<char> host(tot, 0);
+  std::memcpy(host.data() + off[0], m[0].data(), sz[0]);
+  std::memcpy(host.data() + off[1], m[1].data(), sz[1]);
+  std::memcpy(host.data() + off[2], m[2].data(), sz[2]);
+  std::memcpy(host.data() + off[3], mr.data(), sz[3]);
+  std::memcpy(host.data() + off[4], mp.data(), sz[4]);
+  std::memcpy(host.data() + off[5], ob01.data(), sz[5]);
+  std::memcpy(host.data() + off[6], ob12.data(), sz[6]);
+  std::memcpy(host.data() + off[7], zoff.data(), sz[7]);
+  std::memcpy(host.data() + off[8], Td.data(), sz[8]);
+  std::memcpy(host.data() + off[9], a0.data(), sz[9]);
+  std::memcpy(host.data() + off[10], row0.data(), sz[10]);
+  std::memcpy(host.data() + off[11], tp.data(), (size_t)nreq * 8);
+  std::memcpy(host.data() + off[11] + (size_t)nreq * 8, wav0.data(), (size_t)nreq * 8);
+  PTB_CUDA(cudaMemcpyAsync(base, host.data(), tot, cudaMemcpyHostToDevice, d->stream));
+  PTB_CUDA(cudaStreamSynchronize(d->stream));
+  for (int l = 0; l < 3; ++l) p.mask[l] = reinterpret_cast<unsigned char *>(base + off[l]);
+  p.mask_refl = reinterpret_cast<unsigned char *>(base + off[3]);
+  p.mask_post = reinterpret_cast<unsigned char *>(base + off[4]);
+  p.ob01 = reinterpret_cast<int *>(base + off[5]);
+  p.ob12 = reinterpret_cast<int *>(base + off[6]);
+  p.zoff = reinterpret_cast<long long *>(base + off[7]);
+  p.Td = reinterpret_cast<long long *>(base + off[8]);
+  p.a0 = reinterpret_cast<long long *>(base + off[9]);
+  p.row0 = reinterpret_cast<long long *>(base + off[10]);
+  p.tp = reinterpret_cast<long long *>(base + off[11]);
+  p.wav0 = reinterpret_cast<long long *>(base + off[11] + (size_t)nreq * 8);
+  p.table_bytes = tot;
+
+  // activation buffers: grow if needed, then zero (gap rows must read as zeros)
+  const size_t r0 = (size_t)p.R[0], r1 = (size_t)p.R[1], r2 = (size_t)p.R[2];
+  const size_t need_f = r0 * 192 + r0 * 512 + 7 * r1 * 256 + 7 * r2 * 128 + r2 * 80 + 64 * 24;
+  if (need_f * 4 > d->act_bytes) {
+    if (d->act) cudaFree(d->act);
+    d->act = nullptr;
+    d->act_bytes = 0;
+    PTB_CUDA(cudaMalloc(&d->act, need_f * 4));
+    d->act_bytes = need_f * 4;
+  }
+  float *q = static_cast<float *>(d->act);
+  auto take = [&](size_t n) {
+    float *r = q;
+    q += (n + 63) & ~(size_t)63;
+    return r;
+  };
+  d->Z = take(r0 * 192);
+  d->X0 = take(r0 * 512);
+  d->U[0] = take(r1 * 256); d->LU[0] = take(r1 * 256); d->XB[0] = take(r1 * 256);
+  d->XT[0] = take(r1 * 256); d->H[0] = take(r1 * 256); d->ACC[0] = take(r1 * 256);
+  d->OUT1 = take(r1 * 256);
+  d->U[1] = take(r2 * 128); d->LU[1] = take(r2 * 128); d->XB[1] = take(r2 * 128);
+  d->XT[1] = take(r2 * 128); d->H[1] = take(r2 * 128); d->ACC[1] = take(r2 * 128);
+  d->P = take(r2 * 128);
+  d->POST = take(r2 * 80);
+  PTB_CUDA(cudaMemsetAsync(d->act, 0, (size_t)(reinterpret_cast<char *>(q) - static_cast<char *>(d->act)),
+                           d->stream));
+  d->have_plan = true;
+  return 0;
+}
+
+// one conv layer over the ragged rows of a level
+int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act, int64_t rows,
+             int row_off0, int row_step, const EpiParams &e) {
+  ConvLaunch c{};
+  c.act = act;
+  c.act_rows = rows;
+  c.batch = 1;
+  c.w = L.w;
+  c.bn = L.bn;
+  c.g.m_rows = (int)rows;
+  c.g.n_cols = L.n_pad;
+  c.g.cin32 = L.cin32;
+  c.g.ntap = L.ntap;
+  c.g.row_off0 = row_off0;
+  c.g.row_step = row_step;
+  c.g.nkb = L.ntap * (L.cin32 / kBK);
+  c.e = e;
+  c.e.bias = L.b;
+  return launch_conv(c, d->gerr, st);
+}
+
+EpiParams rows_epi(const unsigned char *mask, int ldc) {
+  EpiParams e{};
+  e.mode = EPI_ROWS;
+  e.mask = mask;
+  e.nstore = ldc;
+  e.ldc = ldc;
+  e.ldc1 = ldc;
+  e.alpha1 = kLr;
+  return e;
+}
+
+int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *wav_dev) {
+  const Plan &p = d->plan;
+  const int nreq = (int)p.T.size();
+  // latents -> level-0 rows
+  {
+    dim3 grid((unsigned)((p.max_T + 31) / 32), 192 / 32, (unsigned)nreq);
+    stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.Td, p.a0, d->Z);
+    PTB_CUDA(cudaGetLastError());
+    count_launch();
+  }
+  // conv_pre 192 -> 512, k7 p3, + LeakyRelu
+  {
+    EpiParams e = rows_epi(p.mask[0], 512);
+    e.out1 = d->X0;
+    if (run_conv(d, st, d->pre, d->Z, p.R[0], -3, 1, e)) return -1;
+  }
+  const float *lvl_in = d->X0;
+  for (int s = 0; s < 2; ++s) {
+    const int C = s == 0 ? 256 : 128;
+    const int64_t rin = p.R[s], rout = p.R[s + 1];
+    const unsigned char *mk = p.mask[s + 1];
+    // ups.s: phase-decomposed convT, taps read delay-line rows g - j
+    {
+      EpiParams e = rows_epi(mk, C);
+      e.mode = EPI_ROWS_CONVT;
+      e.obase = s == 0 ? p.ob01 : p.ob12;
+      e.s = 4;
+      e.cphase = C;
+      e.out0 = d->U[s];
+      e.out1 = d->LU[s];
+      if (run_conv(d, st, d->ups[s], lvl_in, rin, 0, -1, e)) return -1;
+    }
+    for (int rb = 0; rb < 3; ++rb) {
+      const int r = 3 * s + rb, K = kK[rb];
+      for (int j = 0; j < 3; ++j) {
+        {  // convs1.j (+ LeakyRelu)
+          EpiParams e = rows_epi(mk, C);
+          e.out1 = d->H[s];
+          const float *in = j == 0 ? d->LU[s] : d->XT[s];
+          if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e)) return -1;
+        }
+        {  // convs2.j + residual (+ leaky for the next stage / branch sum)
+          EpiParams e = rows_epi(mk, C);
+          e.res = j == 0 ? d->U[s] : d->XB[s];
+          if (j < 2) {
+            e.out0 = d->XB[s];
+            e.out1 = d->XT[s];
+          } else if (rb == 0) {
+            e.out0 = d->ACC[s];
+          } else if (rb == 1) {
+            e.accin = d->ACC[s];
+            e.acc_mode = 2;
+            e.out0 = d->ACC[s];
+          } else {
+            e.accin = d->ACC[s];
+            e.acc_mode = 3;
+            if (s == 0) {
+              e.out1 = d->OUT1;
+            } else {
+              e.out1 = d->P;
+              e.alpha1 = kLrFinal;
+              e.mask = p.mask_refl;
+            }
+          }
+          if (run_conv(d, st, d->rb2[r][j], d->H[s], rout, -(K - 1) / 2, 1, e)) return -1;
+        }
+      }
+    }
+    lvl_in = d->OUT1;
+  }
+  // subband_conv_post 128 -> 72 (N tile 80), k7 p3, over the reflection-padded rows
+  {
+    EpiParams e = rows_epi(p.mask_post, 80);
+    e.out0 = d->POST;
+    if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e)) return -1;
+  }
+  return tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, nreq, 16 * p.max_T + 1, d->pqmf, wav_dev, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+pt_b200_decoder *pt_b200_decoder_create(int device, const pt_b200_dec_weights *w) {
+  if (!w) {
+    set_error("pt_b200: NULL decoder weights");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    set_error("pt_b200: cannot select device %d", device);
+    return nullptr;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10 || prop.minor != 0) {
+    set_error("pt_b200: device %d is not sm_100 (B200); this library has no other path", device);
+    return nullptr;
+  }
+  auto *d = new pt_b200_decoder();
+  d->device = device;
+  auto fail = [&](const char *what) {
+    fprintf(stderr, "pt_b200: decoder create failed at %s\n", what);
+    pt_b200_decoder_destroy(d);
+    return static_cast<pt_b200_decoder *>(nullptr);
+  };
+  if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+  if (cudaMalloc(&d->gerr, 4) != cudaSuccess || cudaMemset(d->gerr, 0, 4) != cudaSuccess ||
+      cudaMallocHost(&d->gerr_host, 4) != cudaSuccess)
+    return fail("error word");
+  *d->gerr_host = 0;
+  cudaStream_t st = d->stream;
+  if (make_layer(&d->pre, w->pre_w, w->pre_b, 512, 7, 192, 512, 1 << 30, st)) return fail("conv_pre");
+  for (int s = 0; s < 2; ++s) {
+    const int Cin = s == 0 ? 512 : 256, C = Cin / 2;
+    if (make_layer(&d->ups[s], w->ups_w[s], w->ups_b[s], 4 * C, 4, Cin, C, C, st)) return fail("ups");
+    for (int rb = 0; rb < 3; ++rb)
+      for (int j = 0; j < 3; ++j) {
+        const int r = 3 * s + rb;
+        if (make_layer(&d->rb1[r][j], w->rb_w1[r][j], w->rb_b1[r][j], C, kK[rb], C, C, 1 << 30, st) ||
+            make_layer(&d->rb2[r][j], w->rb_w2[r][j], w->rb_b2[r][j], C, kK[rb], C, C, 1 << 30, st))
+          return fail("resblock");
+      }
+  }
+  if (make_layer(&d->post, w->post_w, w->post_b, 72, 7, 128, 72, 1 << 30, st)) return fail("conv_post");
+  if (cudaMalloc(&d->pqmf, 4 * 63 * 4) != cudaSuccess ||
+      cudaMemcpy(d->pqmf, w->pqmf, 4 * 63 * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail("pqmf");
+  return d;
+}
+
+void pt_b200_decoder_destroy(pt_b200_decoder *d) {
+  if (!d) return;
+  cudaSetDevice(d->device);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  auto fl = [](DLayer &L) {
+    if (L.w) cudaFree(L.w);
+    if (L.b) cudaFree(L.b);
+  };
+  fl(d->pre);
+  fl(d->ups[0]);
+  fl(d->ups[1]);
+  for (int r = 0; r < 6; ++r)
+    for (int j = 0; j < 3; ++j) {
+      fl(d->rb1[r][j]);
+      fl(d->rb2[r][j]);
+    }
+  fl(d->post);
+  if (d->pqmf) cudaFree(d->pqmf);
+  if (d->act) cudaFree(d->act);
+  if (d->plan.table_block) cudaFree(d->plan.table_block);
+  if (d->zbuf) cudaFree(d->zbuf);
+  if (d->wavbuf) cudaFree(d->wavbuf);
+  if (d->gerr) cudaFree(d->gerr);
+  if (d->gerr_host) cudaFreeHost(d->gerr_host);
+  if (d->stream) cudaStreamDestroy(d->stream);
+  delete d;
+}
+
+int pt_b200_decode_batch_device(pt_b200_decoder *d, void *stream, int nreq, const int64_t *T,
+                                const float *z_dev, float *wav_dev) {
+  PTB_REQUIRE(d && T && z_dev && wav_dev && nreq > 0, "pt_b200: bad decode arguments");
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
+  if (build_plan(d, nreq, T)) return -1;
+  if (st != d->stream) {
+    // plan uploads ran on the decoder stream: order them before work on the caller's stream
+    PTB_CUDA(cudaStreamSynchronize(d->stream));
+  }
+  return run_decoder(d, st, z_dev, wav_dev);
+}
+
+int pt_b200_decoder_sync(pt_b200_decoder *d, void *stream) {
+  PTB_REQUIRE(d, "pt_b200: NULL decoder");
+  PTB_CUDA(cudaSetDevice(d->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
+  PTB_CUDA(cudaMemcpyAsync(d->gerr_host, d->gerr, 4, cudaMemcpyDeviceToHost, st));
+  PTB_CUDA(cudaStreamSynchronize(st));
+  if (*d->gerr_host) {
+    set_error("pt_b200: decoder device error word 0x%x", *d->gerr_host);
+    *d->gerr_host = 0;
+    cudaMemset(d->gerr, 0, 4);
+    return -1;
+  }
+  return 0;
+}
+
+int pt_b200_decode_batch(pt_b200_decoder *d, void *stream, int nreq, const int64_t *T,
+                         const float *z_host, float *wav_host) {
+  PTB_REQUIRE(d && T && z_host && wav_host && nreq > 0, "pt_b200: bad decode arguments");
+  int64_t nz = 0, nw = 0;
+  for (int i = 0; i < nreq; ++i) {
+    nz += 192 * T[i];
+    nw += 256 * T[i];
+  }
+  {
+    std::lock_guard<std::mutex> lk(d->mu);
+    PTB_CUDA(cudaSetDevice(d->device));
+    if ((size_t)nz * 4 > d->zbuf_bytes) {
+      if (d->zbuf) cudaFree(d->zbuf);
+      d->zbuf = nullptr;
+      d->zbuf_bytes = 0;
+      PTB_CUDA(cudaMalloc(&d->zbuf, (size_t)nz * 4));
+      d->zbuf_bytes = (size_t)nz * 4;
+    }
+    if ((size_t)nw * 4 > d->wavbuf_bytes) {
+      if (d->wavbuf) cudaFree(d->wavbuf);
+      d->wavbuf = nullptr;
+      d->wavbuf_bytes = 0;
+      PTB_CUDA(cudaMalloc(&d->wavbuf, (size_t)nw * 4));
+      d->wavbuf_bytes = (size_t)nw * 4;
+    }
+  }
+  cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
+  PTB_CUDA(cudaMemcpyAsync(d->zbuf, z_host, (size_t)nz * 4, cudaMemcpyHostToDevice, st));
+  if (pt_b200_decode_batch_device(d, st, nreq, T, d->zbuf, d->wavbuf)) return -1;
+  PTB_CUDA(cudaMemcpyAsync(wav_host, d->wavbuf, (size_t)nw * 4, cudaMemcpyDeviceToHost, st));
+  return pt_b200_decoder_sync(d, st);
+}
+
+int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav) {
+  PTB_REQUIRE(c && c->use_cuda && c->g_stream, "pt_b200: context is not initialised for the GPU");
+  return pt_b200_decode_batch(const_cast<pt_b200_decoder *>(d), c->g_stream, 1, &T, z, wav);
+}
+
+}  // extern "C"

@@ -1,0 +1,112 @@
+"""Parity of the iSTFT+PQMF tail kernel and of the batched device-resident decoder against the
+CPU oracle (which is bit-exact to the reference's CPU path, tests/test_oracle.py).
+
+Gates (tests/v21_reference.py:430-447, 502-505): SNDR >= 60 dB per waveform; the tail alone,
+whose arithmetic follows the reference's operation order, is held much tighter.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import pt_b200
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = pt_b200.Context(0)
+    yield c
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return oracle.CpuDecoder("oracle")
+
+
+@pytest.fixture(scope="module")
+def cfg3():
+    return pt_b200.config3(seed=2, T=226)
+
+
+@pytest.fixture(scope="module")
+def dec(cfg3):
+    d = pt_b200.Decoder(cfg3[0], device=0)
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("Tp", [2, 17, 49, 129, 161, 1000, 3617])
+def test_tail_matches_oracle(ctx, orc, Tp):
+    rng = np.random.default_rng(Tp)
+    post = (0.5 * rng.standard_normal((72, Tp))).astype(np.float32)
+    pq = pt_b200.pqmf_synthesis_filter()
+    ref = orc.tail(post, pq)
+    y = ctx.istft_pqmf(post, pq)
+    m = oracle.metrics(y, ref)
+    # only exp/sin/cos may differ (libm vs CUDA, <= 2 ulp): everything else is order-exact
+    assert m["max_rel"] <= 1e-5 and m["sndr_db"] >= 100, m
+
+
+def test_config3_decoder(dec, orc, cfg3):
+    w, z = cfg3
+    ref = orc.decode(w, z)
+    (y,) = dec.decode([z])
+    assert y.shape == ref.shape == (256 * 226,)
+    m = oracle.metrics(y, ref)
+    print("config 3 decoder vs oracle:", m)
+    assert m["sndr_db"] >= 60.0, m
+
+
+def test_ragged_batch_each_request_matches_oracle(dec, orc, cfg3):
+    w = cfg3[0]
+    rng = np.random.default_rng(11)
+    Ts = [2, 3, 17, 64, 129]
+    zs = [rng.standard_normal((192, t)).astype(np.float32) for t in Ts]
+    outs = dec.decode(zs)
+    for z, y in zip(zs, outs):
+        m = oracle.metrics(y, orc.decode(w, z))
+        assert m["sndr_db"] >= 60.0, (z.shape, m)
+
+
+def test_batch_invariance_bitwise(dec):
+    """A request decodes to the same bits alone or anywhere inside a ragged batch."""
+    rng = np.random.default_rng(12)
+    Ts = [50, 7, 333, 128, 129, 2]
+    zs = [rng.standard_normal((192, t)).astype(np.float32) for t in Ts]
+    together = dec.decode(zs)
+    for i in (0, 2, 5):
+        (alone,) = dec.decode([zs[i]])
+        assert np.array_equal(alone, together[i])
+    again = dec.decode(zs[::-1])[::-1]
+    for a, b in zip(again, together):
+        assert np.array_equal(a, b)
+
+
+def test_config4_batch_properties(dec, orc, cfg3):
+    """The benchmark workload (64 requests, T ~ U{50..600}, seed 3): shapes, finiteness, the two
+    shortest requests against the oracle, and two more against their solo decode."""
+    T, zs = pt_b200.config4()
+    outs = dec.decode(zs)
+    assert [o.size for o in outs] == [256 * t for t in T]
+    assert all(np.isfinite(o).all() for o in outs)
+    order = np.argsort(T)
+    for i in order[:2]:
+        m = oracle.metrics(outs[i], orc.decode(cfg3[0], zs[i]))
+        assert m["sndr_db"] >= 60.0, (T[i], m)
+    for i in order[-2:]:
+        (alone,) = dec.decode([zs[i]])
+        assert np.array_equal(alone, outs[i])
+
+
+def test_decode_single_request_via_context(ctx, dec, cfg3):
+    """pt_v21_decode: the one-request driver shape on an interpreter context."""
+    import ctypes as C
+    z = cfg3[1][:, :40].copy()
+    wav = np.empty(256 * 40, np.float32)
+    f = C.POINTER(C.c_float)
+    rc = pt_b200.lib().pt_v21_decode(ctx.ptr, dec.h, z.ctypes.data_as(f), 40, wav.ctypes.data_as(f))
+    assert rc == 0
+    (ref,) = dec.decode([z])
+    assert np.array_equal(wav, ref)
