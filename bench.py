@@ -1,0 +1,395 @@
+#!/usr/bin/env python
+"""bench.py -- PrimeTTS v2.1 MB-iSTFT decoder on B200: audio-seconds per second per box.
+
+Workload (the configuration the metric is quoted on): 64 concurrent
+decoder requests per GPU, latent lengths T ~ U{50..600} frames (numpy default_rng(3)), the
+config-3 architecture with random-init weights (default_rng(2)).  With N GPUs the job is 64*N
+requests from the same generator, sharded request-parallel by LPT on frames, weights replicated,
+no collective on the data path ("scaling": "weak").  One step = one batched decode of a rank's
+requests (every layer of every request, the iSTFT/PQMF tail included).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`value` is device-resident throughput (z and the waveform in HBM, CUDA events around K steps,
+L2 flushed between steps, max over ranks).  `e2e` is the same metric through the C ABI's host
+entry point (pt_b200_decode_batch): pinned host latents in, host waveform out, copies inside the
+timed region.  `--impl reference` times the reference's own CPU decoder (oracle/_ref, compiled
+from its sources) on all host cores, on a bounded sample of the same workload.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(REPO, "prime-tts_b200"), os.path.join(REPO, "oracle")]
+
+import numpy as np  # noqa: E402
+
+import pt_b200  # noqa: E402
+
+METRIC = "decoder audio-sec/s per box"
+UNIT = "audio-s/s"
+PER_GPU_REQUESTS = 64
+SAMPLE_RATE = 16000
+HOP = 256
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU baseline leg (used for profiler passes)")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="one untimed device decode of the workload, for ncu captures")
+    return ap.parse_args()
+
+
+def lpt_shards(T, n):
+    """Longest-processing-time greedy assignment of requests to n ranks by frames."""
+    loads, shards = [0] * n, [[] for _ in range(n)]
+    for i in sorted(range(len(T)), key=lambda i: -T[i]):
+        g = min(range(n), key=lambda g: loads[g])
+        shards[g].append(i)
+        loads[g] += T[i]
+    return [sorted(s) for s in shards]
+
+
+def workload(n_gpus):
+    T, zs = pt_b200.config4(seed=3, n=PER_GPU_REQUESTS * n_gpus)
+    w, _ = pt_b200.config3(seed=2)
+    return T, zs, w
+
+
+def audio_seconds(frames):
+    return frames * HOP / SAMPLE_RATE
+
+
+def config_dict(n_gpus, T):
+    return {
+        "workload": "BASELINE config 4: 64 concurrent decoder requests per GPU, T~U{50..600} "
+                    "frames (seed 3), config-3 v21_mbistft_16k decoder, random-init weights "
+                    "(seed 2); request-parallel across GPUs (LPT on frames), weights replicated",
+        "requests": len(T),
+        "frames": int(sum(T)),
+        "audio_s": round(audio_seconds(sum(T)), 3),
+        "gflop_per_step": round(sum(pt_b200.decoder_gflop(t) for t in T), 3),
+        "l2": "flushed between timed iterations (256 MiB device write)",
+        "parallelism": f"request-parallel x{n_gpus}, no collective",
+    }
+
+
+# ----------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.p = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.p = None
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self, gpus):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in gpus:
+                continue
+            try:
+                cur, m = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            mx = max(mx, m)
+            if cur > 0.5 * m:   # under load
+                sm.append(cur)
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(self.lines)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def traffic_from_profiles(kernel, flops_per_launch):
+    """DRAM bytes per launch from the committed ncu summary (captured on a smaller case and
+    scaled by algorithmic FLOPs, since the kernel's traffic grows with the rows it processes)."""
+    try:
+        with open(os.path.join(REPO, "profiles", "conv_tc_traffic.json")) as f:
+            d = json.load(f)[kernel]
+        return d["dram_bytes"] * flops_per_launch / d["flops"]
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------------------------------
+def cpu_reference_sample(T, zs, w, threads):
+    """Bounded sample for the reference CPU decoder: one request per host thread, taken from the
+    16 shortest requests of the workload (cycled), all threads in parallel."""
+    order = sorted(range(len(T)), key=lambda i: T[i])[:16]
+    return [order[i % len(order)] for i in range(threads)]
+
+
+def run_cpu_reference(T, zs, w, picks):
+    import oracle
+    kind = "reference" if os.path.exists(oracle.LIB_REF) else "oracle"
+    decs = [oracle.CpuDecoder(kind) for _ in picks]
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=d.decode, args=(w, zs[i])) for d, i in zip(decs, picks)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    return audio_seconds(sum(T[i] for i in picks)) / dt, dt, ("reference" if kind == "reference" else "port")
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_block(T, zs, w):
+    threads = host_threads()
+    picks = cpu_reference_sample(T, zs, w, threads)
+    v, dt, kind = run_cpu_reference(T, zs, w, picks)
+    tp = sorted(set(T[i] for i in picks))
+    return {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{len(picks)} config-4 requests (T in {tp[0]}..{tp[-1]} frames, the 16 "
+                      f"shortest cycled), one per host thread in parallel; {dt:.1f} s wall"}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    T, zs, w = workload(args.gpus)
+    threads = host_threads()
+    picks = cpu_reference_sample(T, zs, w, threads)
+    for _ in range(args.warmup):
+        run_cpu_reference(T, zs, w, picks)
+    times, kind = [], "reference"
+    for _ in range(args.steps):
+        v, dt, kind = run_cpu_reference(T, zs, w, picks)
+        times.append(dt)
+    per_step = audio_seconds(sum(T[i] for i in picks))
+    value = per_step / statistics.mean(times)
+    tp = sorted(set(T[i] for i in picks))
+    sample = (f"{len(picks)} config-4 requests per step (T in {tp[0]}..{tp[-1]}, the 16 shortest "
+              f"cycled), one per host thread")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * statistics.mean(times), 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.gpus, T),
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+# ----------------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    T_all, zs_all, w = workload(world)
+    shard = lpt_shards(T_all, world)[rank]
+    T = np.array([T_all[i] for i in shard], np.int64)
+    zcat = np.concatenate([zs_all[i].ravel() for i in shard])
+    dec = pt_b200.Decoder(w, device=local)
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+    z_dev = torch.from_numpy(zcat).to(dev)
+    wav_dev = torch.empty(int(HOP * T.sum()), device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > L2
+
+    if args.profile_case:
+        dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+        dec.sync(sh)
+        print(json.dumps({"profile_case": True, "requests": len(T), "frames": int(T.sum())}))
+        return 0
+
+    def barrier():
+        if dist:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput ----------------------------------------------------------
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+        dec.sync(sh)
+    dec.profile(True)
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    barrier()
+    pt_b200.kernel_launches(reset=True)
+    total_ms, launches = 0.0, []
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+            e1.record(stream)
+            dec.sync(sh)
+            total_ms += e0.elapsed_time(e1)
+            launches.extend(dec.launch_times())
+    gpu_launches = pt_b200.kernel_launches()
+    barrier()
+    dec.profile(False)
+    t_step = max_over_ranks(total_ms / args.steps) / 1e3
+
+    # ---- end to end through the host entry point (pinned buffers, copies timed) --------------
+    z_host = torch.from_numpy(zcat).pin_memory()
+    wav_host = torch.empty(int(HOP * T.sum()), dtype=torch.float32).pin_memory()
+    dec.decode_host_ptr(T, z_host.data_ptr(), wav_host.data_ptr(), sh)   # warm-up
+    barrier()
+    e2e_ms = 0.0
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.decode_host_ptr(T, z_host.data_ptr(), wav_host.data_ptr(), sh)
+        e1.record(stream)
+        stream.synchronize()
+        e2e_ms += e0.elapsed_time(e1)
+    barrier()
+    t_e2e = max_over_ranks(e2e_ms / args.steps) / 1e3
+    clk = clocks.stop(list(range(world))) if rank == 0 else None
+    ok = np.isfinite(wav_host.numpy()).all()
+
+    if dist:
+        dist.destroy_process_group()
+    if rank != 0:
+        dec.close()
+        return 0
+
+    audio = audio_seconds(sum(T_all))
+    # roofline of the dominant kernel instance, from the live per-launch events
+    groups = {}
+    for kind, bn, ms, fl, by in launches:
+        name = f"conv_tc_kernel<{bn}>" if bn else f"{kind}_kernel"
+        g = groups.setdefault(name, [0.0, 0.0, 0.0, 0])
+        g[0] += ms
+        g[1] += fl
+        g[2] += by
+        g[3] += 1
+    tot = sum(g[0] for g in groups.values())
+    dom = max(groups, key=lambda k: groups[k][0])
+    peaks, peak_src = measured_peaks()
+    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    g = groups[dom]
+    if dom.startswith("conv_tc"):
+        achieved = g[1] / (g[0] / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
+                "traffic": traffic_from_profiles(dom, g[1] / g[3])}
+    else:
+        achieved = g[2] / (g[0] / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None}
+    roof["kernel"] = dom
+    roof["share"] = round(g[0] / tot, 4)
+    roof["peak_source"] = (f"{peak_src} MEASURED_PEAKS bf16_tflops_sustained "
+                           f"{peaks['bf16_tflops_sustained']} / 2 (kind::tf32 rate)")
+    conv_ms = sum(v[0] for k, v in groups.items() if k.startswith("conv_tc"))
+    conv_fl = sum(v[1] for k, v in groups.items() if k.startswith("conv_tc"))
+    conv_tflops = conv_fl / (conv_ms / 1e3) / 1e12
+    kernels = {k: {"ms_per_step": round(v[0] / args.steps, 4), "share": round(v[0] / tot, 4),
+                   "launches_per_step": v[3] // args.steps,
+                   "tflops": round(v[1] / (v[0] / 1e3) / 1e12, 1) if v[1] else None}
+               for k, v in sorted(groups.items(), key=lambda kv: -kv[1][0])}
+
+    out = {
+        "metric": METRIC, "value": round(audio / t_step, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "tf32 (tensor-core operands, round-to-nearest), fp32 accumulate/epilogues",
+        "data": "synthetic (seeded N(0,1) latents, N(0,0.02^2) weights)",
+        "config": config_dict(world, T_all),
+        "conv_tflops": round(conv_tflops, 1),
+        "conv_tf32_frac": round(conv_tflops / tf32_peak, 4),
+        "roofline": roof,
+        "kernels": kernels,
+        "e2e": {"value": round(audio / t_e2e, 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(zcat.nbytes), "d2h_bytes_per_step": int(wav_host.numel() * 4),
+                "ms_per_step": round(t_e2e * 1e3, 3), "output_finite": bool(ok)},
+        "gpu_launches": int(gpu_launches),
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_block(T_all, zs_all, w)
+    dec.close()
+    print(json.dumps(out))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

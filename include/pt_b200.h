@@ -239,6 +239,17 @@ PT_B200_API int pt_b200_decode_batch_device(pt_b200_decoder *d, void *stream, in
                                 const float *z_dev, float *wav_dev);
 PT_B200_API int pt_b200_decoder_sync(pt_b200_decoder *d, void *stream);
 
+/* Live per-launch timing of the decoder, for the benchmark's roofline: with profiling enabled
+ * every decode records a CUDA event before each of its launches (and one after the last) on the
+ * decode stream.  After the decode has been synchronised, pt_b200_decoder_launch_times fills, per
+ * launch of that decode: its duration in ms, its algorithmic FLOPs and bytes, and its kind
+ * (low byte: 0 latent staging, 1 conv, 2 upsampler convT, 3 conv_post, 4 iSTFT+PQMF tail; bits
+ * 8..: the N tile of the tensor-core conv instance, 0 for other kernels); it returns the number
+ * of launches. */
+PT_B200_API int pt_b200_decoder_profile(pt_b200_decoder *d, int enable);
+PT_B200_API int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double *ms,
+                                             double *flops, double *bytes, int *kind);
+
 /* One request, the reference's driver shape (an extension the survey lists as pt_v21_decode):
  * z [192][T] host -> wav [256*T] host. */
 PT_B200_API int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav);

@@ -41,7 +41,8 @@ inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
 // ---- TMA tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point, so the
 // library does not link libcuda directly)
-int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int batch);
+int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int batch,
+                 int box_rows);
 int make_map_w(CUtensorMap *m, const float *base, int64_t krow, int64_t nrows, int box_n);
 
 // ---- the tensor-core conv: picks the N tile instance and launches

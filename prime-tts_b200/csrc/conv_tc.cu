@@ -1,6 +1,8 @@
 // conv_tc.cu -- instances of the tensor-core conv kernel, TMA map encoding, error plumbing.
 #include <cudaTypedefs.h>
 
+#include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -44,7 +46,8 @@ static int encoder(PFN_cuTensorMapEncodeTiled_v12000 *fn) {
   return 0;
 }
 
-int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int batch) {
+int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int batch,
+                 int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   if (encoder(&enc)) return -1;
   PTB_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0 && cin32 % kBK == 0 && rows > 0 &&
@@ -52,7 +55,7 @@ int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int
               "pt_b200: activation map needs a 16-byte aligned base and 32-channel rows");
   cuuint64_t dims[3] = {(cuuint64_t)cin32, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)cin32 * 4, (cuuint64_t)cin32 * 4 * (cuuint64_t)rows};
-  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)kBM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -97,7 +100,7 @@ static int launch_bn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   });
   PTB_CUDA(attr_err);
   CUtensorMap ta, tb;
-  if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch)) return -1;
+  if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kBM)) return -1;
   if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
   dim3 grid((unsigned)((L.g.m_rows + kBM - 1) / kBM), (unsigned)(L.g.n_cols / BN),
             (unsigned)L.batch);
@@ -107,7 +110,89 @@ static int launch_bn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   return 0;
 }
 
-static const int kTiles[] = {16, 32, 64, 80, 128, 256};
+template <int BN, int MSUB>
+static int launch_win(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
+  using W = WinCfg<BN, MSUB>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(conv_tc_win_kernel<BN, MSUB>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, W::kBytes);
+  });
+  PTB_CUDA(attr_err);
+  CUtensorMap ta, tb;
+  if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
+  if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
+  dim3 grid((unsigned)((L.g.m_rows + MSUB * kBM - 1) / (MSUB * kBM)), (unsigned)(L.g.n_cols / BN),
+            (unsigned)L.batch);
+  conv_tc_win_kernel<BN, MSUB><<<grid, kThreads, W::kBytes, st>>>(ta, tb, L.g, L.e, gerr);
+  PTB_CUDA(cudaGetLastError());
+  count_launch();
+  return 0;
+}
+
+// Rows per CTA: the largest tile that does not cost extra waves on the SMs (a tile of MSUB*128
+// rows is modelled as MSUB + 0.5 units of time: mainloop plus fixed set-up/epilogue).
+static int pick_msub(const ConvLaunch &L, const int *cands, int ncand) {
+  static int forced = -2;
+  if (forced == -2) forced = getenv("PT_B200_MSUB") ? atoi(getenv("PT_B200_MSUB")) : 0;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  int best = cands[0];
+  double best_t = 1e300;
+  for (int i = 0; i < ncand; ++i) {
+    const int ms = cands[i];
+    if (forced > 0 && ms == forced) return ms;
+    const double tiles = (double)((L.g.m_rows + ms * kBM - 1) / (ms * kBM)) * (L.g.n_cols / L.bn) * L.batch;
+    const double waves = std::ceil(tiles / sms);
+    const double t = waves * (ms + 0.5);
+    if (t < best_t - 1e-9 || (std::fabs(t - best_t) < 1e-9 && ms > best)) {
+      best_t = t;
+      best = ms;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
+  using P = PersCfg<BN>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(conv_tc_pers_kernel<BN>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, P::kBytes);
+  });
+  PTB_CUDA(attr_err);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  CUtensorMap ta, tb;
+  if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
+  if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
+  const long long tiles = (long long)((L.g.m_rows + kPMsub * kBM - 1) / (kPMsub * kBM)) *
+                          (L.g.n_cols / BN) * L.batch;
+  ConvGeom g = L.g;
+  g.nbatch = L.batch;
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  conv_tc_pers_kernel<BN><<<grid, kPThreads, P::kBytes, st>>>(ta, tb, g, L.e, gerr);
+  PTB_CUDA(cudaGetLastError());
+  count_launch();
+  return 0;
+}
+
+// N tiles: up to 128 columns per tile (two accumulator sets then fit TMEM); wider layers are
+// split into 128-column tiles.
+static const int kTiles[] = {16, 32, 64, 80, 128};
 
 int pick_bn(int ncols, int *bn, int *n_pad) {
   PTB_REQUIRE(ncols > 0, "pt_b200: empty N extent");
@@ -118,8 +203,8 @@ int pick_bn(int ncols, int *bn, int *n_pad) {
       *n_pad = t;
       return 0;
     }
-  *bn = 256;
-  *n_pad = (int)round_up(ncols, 256);
+  *bn = 128;
+  *n_pad = (int)round_up(ncols, 128);
   return 0;
 }
 
@@ -127,13 +212,34 @@ int launch_conv(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   PTB_REQUIRE(L.g.m_rows > 0 && L.g.nkb > 0 && L.g.n_cols % L.bn == 0,
               "pt_b200: bad conv geometry (m=%d nkb=%d n=%d bn=%d)", L.g.m_rows, L.g.nkb,
               L.g.n_cols, L.bn);
+  static int no_win = -1;
+  if (no_win < 0) no_win = getenv("PT_B200_NO_WINDOW") ? atoi(getenv("PT_B200_NO_WINDOW")) : 0;
+  const int halo = std::abs((L.g.ntap - 1) * L.g.row_step);
+  static int no_pers = -1;
+  if (no_pers < 0) no_pers = getenv("PT_B200_NO_PERSIST") ? atoi(getenv("PT_B200_NO_PERSIST")) : 0;
+  if (!no_win && halo <= kWinHalo) {
+    if (!no_pers) {
+      if (L.bn == 128) return launch_pers<128>(L, gerr, st);
+      if (L.bn == 80) return launch_pers<80>(L, gerr, st);
+    }
+    static const int c24[] = {2, 4};
+    switch (L.bn) {
+      case 128: return pick_msub(L, c24, 2) == 2 ? launch_win<128, 2>(L, gerr, st)
+                                                 : launch_win<128, 4>(L, gerr, st);
+      case 80: return pick_msub(L, c24, 2) == 2 ? launch_win<80, 2>(L, gerr, st)
+                                               : launch_win<80, 4>(L, gerr, st);
+      case 64: return launch_win<64, 2>(L, gerr, st);
+      case 32: return launch_win<32, 2>(L, gerr, st);
+      case 16: return launch_win<16, 2>(L, gerr, st);
+      default: break;
+    }
+  }
   switch (L.bn) {
     case 16: return launch_bn<16>(L, gerr, st);
     case 32: return launch_bn<32>(L, gerr, st);
     case 64: return launch_bn<64>(L, gerr, st);
     case 80: return launch_bn<80>(L, gerr, st);
     case 128: return launch_bn<128>(L, gerr, st);
-    case 256: return launch_bn<256>(L, gerr, st);
     default: set_error("pt_b200: no conv instance for N tile %d", L.bn); return -1;
   }
 }

@@ -118,6 +118,13 @@ struct pt_b200_decoder {
   float *U[2], *LU[2], *XB[2], *XT[2], *H[2], *ACC[2], *OUT1 = nullptr, *P = nullptr, *POST = nullptr;
   float *zbuf = nullptr, *wavbuf = nullptr;  // staging for the host-buffer entry point
   size_t zbuf_bytes = 0, wavbuf_bytes = 0;
+  // live per-launch timing (pt_b200_decoder_profile): one event before each launch, one at the end
+  static constexpr int kMaxRec = 64;
+  bool prof = false;
+  cudaEvent_t ev[kMaxRec + 1] = {};
+  int nrec = 0;
+  int rkind[kMaxRec] = {};
+  double rflops[kMaxRec] = {}, rbytes[kMaxRec] = {};
 };
 
 namespace {
@@ -275,6 +282,19 @@ int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *
   return launch_conv(c, d->gerr, st);
 }
 
+// launch kinds reported by pt_b200_decoder_launch_times
+enum { LK_STAGE = 0, LK_CONV = 1, LK_CONVT = 2, LK_POST = 3, LK_TAIL = 4 };
+
+// kind | (N tile << 8): the N tile names the conv kernel instance the launch used
+void rec(pt_b200_decoder *d, cudaStream_t st, int kind, double flops, double bytes, int bn = 0) {
+  if (!d->prof || d->nrec >= pt_b200_decoder::kMaxRec) return;
+  cudaEventRecord(d->ev[d->nrec], st);
+  d->rkind[d->nrec] = kind | (bn << 8);
+  d->rflops[d->nrec] = flops;
+  d->rbytes[d->nrec] = bytes;
+  ++d->nrec;
+}
+
 EpiParams rows_epi(const unsigned char *mask, int ldc) {
   EpiParams e{};
   e.mode = EPI_ROWS;
@@ -289,7 +309,13 @@ EpiParams rows_epi(const unsigned char *mask, int ldc) {
 int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *wav_dev) {
   const Plan &p = d->plan;
   const int nreq = (int)p.T.size();
+  d->nrec = 0;
+  double frames = 0;  // sum of latent frames over the batch
+  for (int64_t t : p.T) frames += (double)t;
+  // algorithmic work of one conv layer over every request's valid rows (2 x MACs)
+  auto cflops = [&](double rows, int cin, int cout, int K) { return 2.0 * rows * cin * cout * K; };
   // latents -> level-0 rows
+  rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
     dim3 grid((unsigned)((p.max_T + 31) / 32), 192 / 32, (unsigned)nreq);
     stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.Td, p.a0, d->Z);
@@ -297,6 +323,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     count_launch();
   }
   // conv_pre 192 -> 512, k7 p3, + LeakyRelu
+  rec(d, st, LK_CONV, cflops(frames, 192, 512, 7), frames * (192 + 512) * 4, d->pre.bn);
   {
     EpiParams e = rows_epi(p.mask[0], 512);
     e.out1 = d->X0;
@@ -308,6 +335,8 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     const int64_t rin = p.R[s], rout = p.R[s + 1];
     const unsigned char *mk = p.mask[s + 1];
     // ups.s: phase-decomposed convT, taps read delay-line rows g - j
+    const double fin = frames * (s == 0 ? 1 : 4), fout = 4 * fin;
+    rec(d, st, LK_CONVT, cflops(fin, 2 * C, C, 16), fin * 2 * C * 4 + fout * 2 * C * 4, d->ups[s].bn);
     {
       EpiParams e = rows_epi(mk, C);
       e.mode = EPI_ROWS_CONVT;
@@ -321,12 +350,14 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     for (int rb = 0; rb < 3; ++rb) {
       const int r = 3 * s + rb, K = kK[rb];
       for (int j = 0; j < 3; ++j) {
+        rec(d, st, LK_CONV, cflops(fout, C, C, K), fout * 2 * C * 4, d->rb1[r][j].bn);
         {  // convs1.j (+ LeakyRelu)
           EpiParams e = rows_epi(mk, C);
           e.out1 = d->H[s];
           const float *in = j == 0 ? d->LU[s] : d->XT[s];
           if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e)) return -1;
         }
+        rec(d, st, LK_CONV, cflops(fout, C, C, K), fout * 4 * C * 4, d->rb2[r][j].bn);
         {  // convs2.j + residual (+ leaky for the next stage / branch sum)
           EpiParams e = rows_epi(mk, C);
           e.res = j == 0 ? d->U[s] : d->XB[s];
@@ -357,12 +388,19 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     lvl_in = d->OUT1;
   }
   // subband_conv_post 128 -> 72 (N tile 80), k7 p3, over the reflection-padded rows
+  const double fpost = 16 * frames + nreq;
+  rec(d, st, LK_POST, cflops(fpost, 128, 72, 7), fpost * (128 + 80) * 4, d->post.bn);
   {
     EpiParams e = rows_epi(p.mask_post, 80);
     e.out0 = d->POST;
     if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e)) return -1;
   }
-  return tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, nreq, 16 * p.max_T + 1, d->pqmf, wav_dev, st);
+  // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
+  rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);
+  if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, nreq, 16 * p.max_T + 1, d->pqmf, wav_dev, st))
+    return -1;
+  if (d->prof) cudaEventRecord(d->ev[d->nrec], st);
+  return 0;
 }
 
 }  // namespace
@@ -439,6 +477,8 @@ void pt_b200_decoder_destroy(pt_b200_decoder *d) {
   if (d->wavbuf) cudaFree(d->wavbuf);
   if (d->gerr) cudaFree(d->gerr);
   if (d->gerr_host) cudaFreeHost(d->gerr_host);
+  for (auto &e : d->ev)
+    if (e) cudaEventDestroy(e);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
 }
@@ -503,6 +543,34 @@ int pt_b200_decode_batch(pt_b200_decoder *d, void *stream, int nreq, const int64
   if (pt_b200_decode_batch_device(d, st, nreq, T, d->zbuf, d->wavbuf)) return -1;
   PTB_CUDA(cudaMemcpyAsync(wav_host, d->wavbuf, (size_t)nw * 4, cudaMemcpyDeviceToHost, st));
   return pt_b200_decoder_sync(d, st);
+}
+
+int pt_b200_decoder_profile(pt_b200_decoder *d, int enable) {
+  PTB_REQUIRE(d, "pt_b200: NULL decoder");
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  if (enable && !d->ev[0])
+    for (int i = 0; i <= pt_b200_decoder::kMaxRec; ++i) PTB_CUDA(cudaEventCreate(&d->ev[i]));
+  d->prof = enable != 0;
+  d->nrec = 0;
+  return 0;
+}
+
+int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double *ms, double *flops,
+                                 double *bytes, int *kind) {
+  PTB_REQUIRE(d && d->prof, "pt_b200: decoder profiling is off");
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  const int n = d->nrec < max ? d->nrec : max;
+  for (int i = 0; i < n; ++i) {
+    float t = 0.0f;
+    PTB_CUDA(cudaEventElapsedTime(&t, d->ev[i], d->ev[i + 1]));
+    ms[i] = t;
+    flops[i] = d->rflops[i];
+    bytes[i] = d->rbytes[i];
+    kind[i] = d->rkind[i];
+  }
+  return n;
 }
 
 int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav) {

@@ -120,6 +120,10 @@ _SIGS = {
     "pt_b200_decode_batch_device": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p,
                                      C.c_void_p], C.c_int),
     "pt_b200_decoder_sync": ([C.c_void_p, C.c_void_p], C.c_int),
+    "pt_b200_decoder_profile": ([C.c_void_p, C.c_int], C.c_int),
+    "pt_b200_decoder_launch_times": ([C.c_void_p, C.c_int, C.POINTER(C.c_double),
+                                      C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                      C.POINTER(C.c_int)], C.c_int),
     "pt_b200_last_error": ([], C.c_char_p),
     "pt_b200_kernel_launches": ([C.c_int], C.c_long),
 }
@@ -458,3 +462,21 @@ class Decoder:
 
     def sync(self, stream=None) -> None:
         _check(lib().pt_b200_decoder_sync(self.h, stream), "pt_b200_decoder_sync")
+
+    LAUNCH_KINDS = ("stage", "conv", "convT", "conv_post", "tail")
+
+    def profile(self, enable: bool) -> None:
+        _check(lib().pt_b200_decoder_profile(self.h, int(enable)), "pt_b200_decoder_profile")
+
+    def launch_times(self) -> list:
+        """[(kind, N tile, ms, algorithmic flops, algorithmic bytes)] for each launch of the last
+        decode (call after sync; profiling must be on).  The N tile names the tensor-core conv
+        instance (conv_tc_kernel<N tile, stages>), 0 for the other kernels."""
+        n = 64
+        ms, fl, by = (C.c_double * n)(), (C.c_double * n)(), (C.c_double * n)()
+        kd = (C.c_int * n)()
+        k = lib().pt_b200_decoder_launch_times(self.h, n, ms, fl, by, kd)
+        if k < 0:
+            _check(k, "pt_b200_decoder_launch_times")
+        return [(self.LAUNCH_KINDS[kd[i] & 255], kd[i] >> 8, ms[i], fl[i], by[i])
+                for i in range(k)]

@@ -73,7 +73,8 @@ def test_convT_cases(ctx, orc, i):
 # the decoder's own conv shapes at a ragged length (tiles partly filled, T not a multiple of 128)
 @pytest.mark.parametrize("cin,cout,K,dil,T", [(192, 512, 7, 1, 226), (256, 256, 11, 5, 300),
                                                (128, 128, 3, 3, 1000), (128, 72, 7, 1, 161),
-                                               (256, 256, 7, 3, 129), (128, 128, 11, 1, 5)])
+                                               (256, 256, 7, 3, 129), (128, 128, 11, 1, 5),
+                                               (64, 64, 15, 5, 200)])   # halo 70: per-tap kernel
 def test_decoder_conv_shapes(ctx, orc, cin, cout, K, dil, T):
     x, wp, b = conv_inputs(7 * cin + K + T, 1, cin, cout, K, T)
     pad = dil * (K - 1) // 2
