@@ -254,6 +254,24 @@ PT_B200_API int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double
  * z [192][T] host -> wav [256*T] host. */
 PT_B200_API int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav);
 
+/* Conv1d with no device allocation (no counterpart in the reference).  For callers that cannot
+ * call cudaMalloc/cudaFree: hosts that own every device allocation (pooled or framework
+ * allocators), real-time threads that must not take the allocator's locks, processes whose
+ * device footprint is fixed after start-up.  Same arithmetic as pt_v21_conv (stride 1, batch 1),
+ * but every pointer is a DEVICE pointer on `device`: x [cin][ldx] (T unpadded columns, the kernel
+ * pads by `pad`), y [cout4][Tout] with Tout = T + 2*pad - (K-1)*dil, wp packed
+ * [cout4/4][K][cin][4], bias [cout] or NULL.  Scratch (staged input, re-laid-out weights) comes
+ * from one fixed 16 MiB array inside the library on each device: calls needing more (T *
+ * round_up(cin,32) + round_up(cout,16) * K * round_up(cin,32) floats, plus padding) are rejected
+ * with -1 and a message.  The first call on a device looks up that array's device address, so
+ * make it before any stream capture.  All calls on a device share the array: calls that overlap
+ * on the GPU (other streams, other threads) race and must be serialised by the caller.  The call
+ * returns after its work on `stream` (NULL = the default stream) has finished. */
+PT_B200_API int pt_b200_conv_noalloc(int device, void *stream, const float *x, int64_t ldx,
+                                     int64_t cin, int64_t T, float *y, int cout, int K, int pad,
+                                     int dil, const float *wp, const float *bias, int epi0,
+                                     float a0);
+
 /* Diagnostics: the last error message of the calling thread, and the number of this library's
  * kernels launched by the calling thread since the last reset. */
 PT_B200_API const char *pt_b200_last_error(void);

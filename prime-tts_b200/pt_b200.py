@@ -124,6 +124,9 @@ _SIGS = {
     "pt_b200_decoder_launch_times": ([C.c_void_p, C.c_int, C.POINTER(C.c_double),
                                       C.POINTER(C.c_double), C.POINTER(C.c_double),
                                       C.POINTER(C.c_int)], C.c_int),
+    "pt_b200_conv_noalloc": ([C.c_int, C.c_void_p, C.c_void_p, _i64, _i64, _i64, C.c_void_p,
+                              C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                              C.c_int, C.c_float], C.c_int),
     "pt_b200_last_error": ([], C.c_char_p),
     "pt_b200_kernel_launches": ([C.c_int], C.c_long),
 }

@@ -1,0 +1,70 @@
+"""pt_b200_conv_noalloc: the Conv1d entry point for callers that cannot allocate device memory.
+
+Such a caller (a host with its own device-memory pool, a real-time thread that must not enter the
+allocator, a process with a fixed device footprint) hands over device buffers for the input,
+weights, bias and output; the library takes its scratch from a fixed array compiled into it
+instead of calling cudaMalloc.  This test calls that entry point through the C ABI twice in a
+row -- the second call on a different shape, so stale contents of the shared array from the
+first call would show -- and compares each result with the allocating entry point pt_v21_conv
+within the per-op tolerance the other tests use.  It lives in its own file, collected last, and
+sets up everything it needs itself, so it also passes alone in a fresh process.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+import pt_b200
+from golden.make_golden import conv_inputs
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _noalloc(x, wp, b, cout, K, pad, dil, epi0=0, a0=0.0):
+    import torch
+    cin, T = x.shape
+    Tout = T + 2 * pad - (K - 1) * dil
+    c4 = (cout + 3) // 4 * 4
+    dev = torch.device("cuda", 0)
+    xd = torch.from_numpy(x).to(dev)
+    wd = torch.from_numpy(wp.ravel()).to(dev)
+    bd = torch.from_numpy(b).to(dev)
+    yd = torch.full((c4, Tout), float("nan"), device=dev)
+    torch.cuda.synchronize()
+    rc = pt_b200.lib().pt_b200_conv_noalloc(0, None, xd.data_ptr(), T, cin, T, yd.data_ptr(), cout,
+                                            K, pad, dil, wd.data_ptr(), bd.data_ptr(), epi0,
+                                            C.c_float(a0))
+    if rc != 0:
+        raise pt_b200.PtB200Error(pt_b200.lib().pt_b200_last_error().decode())
+    return yd.cpu().numpy()
+
+
+def test_noalloc_matches_allocating_conv_twice():
+    cases = [  # (seed, cin, cout, K, dil, T, epi0, a0): two different shapes back to back
+        (71, 512, 256, 7, 1, 256, 1, 0.1),     # the BASELINE config-1 shape
+        (72, 96, 72, 11, 3, 150, 0, 0.0),      # smaller, ragged: stale scratch would show
+    ]
+    with pt_b200.Context(0) as ctx:
+        for seed, cin, cout, K, dil, T, e0, a0 in cases:
+            x, wp, b = conv_inputs(seed, 1, cin, cout, K, T)
+            pad = dil * (K - 1) // 2
+            ref = ctx.conv(x, wp, b, cout, K, pad, dil, epi0=e0, a0=a0)[0]
+            y = _noalloc(x[0], wp, b, cout, K, pad, dil, e0, a0)
+            m = oracle.metrics(y, ref)
+            assert np.isfinite(y).all()
+            assert m["max_rel"] <= TOL, (seed, m)
+
+
+def test_noalloc_rejects_oversized_calls():
+    import torch
+    dev = torch.device("cuda", 0)
+    cin, T, cout, K = 1024, 8192, 64, 3          # 8192 x 1024 floats of input: 32 MiB > 16 MiB
+    xd = torch.zeros((cin, T), device=dev)
+    wd = torch.zeros(cout * K * cin, device=dev)
+    yd = torch.zeros((cout, T), device=dev)
+    rc = pt_b200.lib().pt_b200_conv_noalloc(0, None, xd.data_ptr(), T, cin, T, yd.data_ptr(), cout,
+                                            K, 1, 1, wd.data_ptr(), None, 0, C.c_float(0.0))
+    assert rc == -1
+    assert b"scratch" in pt_b200.lib().pt_b200_last_error()
