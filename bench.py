@@ -335,7 +335,8 @@ def main():
     # roofline of the dominant kernel instance, from the live per-launch events
     groups = {}
     for kind, bn, ms, fl, by in launches:
-        name = f"conv_tc_kernel<{bn}>" if bn else f"{kind}_kernel"
+        name = ("conv_tc_tn_kernel" if bn == 128 else f"conv_tc_win_kernel<{bn}>") if bn \
+            else f"{kind}_kernel"
         g = groups.setdefault(name, [0.0, 0.0, 0.0, 0])
         g[0] += ms
         g[1] += fl

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 
+#define PTB_CONV_KERNELS
 #include "common.cuh"
 
 namespace ptb {
@@ -190,9 +191,70 @@ static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   return 0;
 }
 
-// N tiles: up to 128 columns per tile (two accumulator sets then fit TMEM); wider layers are
-// split into 128-column tiles.
-static const int kTiles[] = {16, 32, 64, 80, 128};
+template <int MODE, int F>
+static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(conv_tc_tn_kernel<MODE, F>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg::kBytes);
+  });
+  PTB_CUDA(attr_err);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  CUtensorMap tx, tw;
+  if (make_map_act(&tx, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
+  if (make_map_w(&tw, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, kBM)) return -1;
+  const long long tiles = (long long)((L.g.n_cols + kBM - 1) / kBM) *
+                          ((L.g.m_rows + kTNRows - 1) / kTNRows) * L.batch;
+  ConvGeom g = L.g;
+  g.nbatch = L.batch;
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg::kBytes, st>>>(tx, tw, g, L.e, gerr);
+  PTB_CUDA(cudaGetLastError());
+  count_launch();
+  return 0;
+}
+
+// The decoder's epilogue combinations get their own instances; anything else runs the generic
+// instance, which reads the same choices from EpiParams at run time.
+static int launch_tn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
+  const EpiParams &e = L.e;
+  if (e.mode == EPI_PLAIN_CONV) return launch_tn_mode<EPI_PLAIN_CONV, 0>(L, gerr, st);
+  if (e.mode == EPI_PLAIN_CONVT) return launch_tn_mode<EPI_PLAIN_CONVT, 0>(L, gerr, st);
+  const int f = (e.res ? EF_RES : 0) | (e.acc_mode == 2 ? EF_ACC2 : 0) |
+                (e.acc_mode == 3 ? EF_ACC3 : 0) | (e.out0 ? EF_OUT0 : 0) |
+                (e.out1 ? EF_OUT1 : 0) | (e.refl ? EF_REFL : 0);
+  if (e.mode == EPI_ROWS_CONVT) {
+    if (f == (EF_OUT0 | EF_OUT1)) return launch_tn_mode<EPI_ROWS_CONVT, EF_OUT0 | EF_OUT1>(L, gerr, st);
+    return launch_tn_mode<EPI_ROWS_CONVT, EF_GENERIC>(L, gerr, st);
+  }
+  if (e.mode != EPI_ROWS) {
+    set_error("pt_b200: unknown epilogue mode %d", e.mode);
+    return -1;
+  }
+  switch (f) {
+    case EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_OUT1>(L, gerr, st);
+    case EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_OUT0>(L, gerr, st);
+    case EF_RES | EF_OUT0 | EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_RES | EF_OUT0 | EF_OUT1>(L, gerr, st);
+    case EF_RES | EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_RES | EF_OUT0>(L, gerr, st);
+    case EF_RES | EF_ACC2 | EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC2 | EF_OUT0>(L, gerr, st);
+    case EF_RES | EF_ACC3 | EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC3 | EF_OUT1>(L, gerr, st);
+    case EF_RES | EF_ACC3 | EF_OUT1 | EF_REFL:
+      return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC3 | EF_OUT1 | EF_REFL>(L, gerr, st);
+    default: return launch_tn_mode<EPI_ROWS, EF_GENERIC>(L, gerr, st);
+  }
+}
+
+// Weight rows (output channels, or phases x channels) per tile.  Up to 64 rows: one N tile of
+// the time-on-M kernels; more: 128-row M tiles of the channels-on-M kernel (weights padded to a
+// multiple of 128 rows).
+static const int kTiles[] = {16, 32, 64};
 
 int pick_bn(int ncols, int *bn, int *n_pad) {
   PTB_REQUIRE(ncols > 0, "pt_b200: empty N extent");
@@ -217,17 +279,17 @@ int launch_conv(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   const int halo = std::abs((L.g.ntap - 1) * L.g.row_step);
   static int no_pers = -1;
   if (no_pers < 0) no_pers = getenv("PT_B200_NO_PERSIST") ? atoi(getenv("PT_B200_NO_PERSIST")) : 0;
+  static int no_tn = -1;
+  if (no_tn < 0) no_tn = getenv("PT_B200_NO_TN") ? atoi(getenv("PT_B200_NO_TN")) : 0;
   if (!no_win && halo <= kWinHalo) {
-    if (!no_pers) {
-      if (L.bn == 128) return launch_pers<128>(L, gerr, st);
-      if (L.bn == 80) return launch_pers<80>(L, gerr, st);
+    if (L.bn == 128) {
+      if (!no_tn) return launch_tn(L, gerr, st);
+      if (!no_pers) return launch_pers<128>(L, gerr, st);
+      static const int c24[] = {2, 4};
+      return pick_msub(L, c24, 2) == 2 ? launch_win<128, 2>(L, gerr, st)
+                                       : launch_win<128, 4>(L, gerr, st);
     }
-    static const int c24[] = {2, 4};
     switch (L.bn) {
-      case 128: return pick_msub(L, c24, 2) == 2 ? launch_win<128, 2>(L, gerr, st)
-                                                 : launch_win<128, 4>(L, gerr, st);
-      case 80: return pick_msub(L, c24, 2) == 2 ? launch_win<80, 2>(L, gerr, st)
-                                               : launch_win<80, 4>(L, gerr, st);
       case 64: return launch_win<64, 2>(L, gerr, st);
       case 32: return launch_win<32, 2>(L, gerr, st);
       case 16: return launch_win<16, 2>(L, gerr, st);
@@ -238,7 +300,6 @@ int launch_conv(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
     case 16: return launch_bn<16>(L, gerr, st);
     case 32: return launch_bn<32>(L, gerr, st);
     case 64: return launch_bn<64>(L, gerr, st);
-    case 80: return launch_bn<80>(L, gerr, st);
     case 128: return launch_bn<128>(L, gerr, st);
     default: set_error("pt_b200: no conv instance for N tile %d", L.bn); return -1;
   }

@@ -68,6 +68,14 @@ struct EpiParams {
   int ldc, ldc1;
   int acc_mode;               // 0 none, 2: v = accin + v, 3: v = (accin + v) / 3
   float alpha1;
+  int refl;                   // rows marked bit1 in mask are also written to row - 2
+};
+
+// Compile-time shape of a decoder epilogue (the TN kernel is instantiated per combination, so
+// each instance carries only the straight-line code it needs).
+enum EpiFlags : int {
+  EF_RES = 1, EF_ACC2 = 2, EF_ACC3 = 4, EF_OUT0 = 8, EF_OUT1 = 16, EF_REFL = 32,
+  EF_GENERIC = -1,   // decide everything at run time from EpiParams
 };
 
 __device__ __forceinline__ float epi_op(float v, int op, float a) {
@@ -95,6 +103,7 @@ struct ConvSmem {
   static constexpr int kBytes = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+#ifdef PTB_CONV_KERNELS   // kernel bodies: compiled in conv_tc.cu only
 // Epilogue for one 32-column chunk held by this thread (its TMEM lane = tile row).
 template <int BN>
 __device__ __forceinline__ void epilogue_chunk(const EpiParams &e, const float (&acc)[32], int z,
@@ -859,5 +868,338 @@ __global__ void __launch_bounds__(kPThreads, 1)
     tmem_dealloc(tmem, 512);
   }
 }
+
+
+// ---------------------------------------------------------------------------------------------
+// Channels-on-M variant ("TN"): D[co][t] = W[co][k] . X[t][k].
+//
+// The MMA is M = 128 output channels (weights, A operand) x N = 256 time rows (the activation
+// window, B operand) x K = 8.  With 4-byte operands, M128 x N128 MMAs need ~122 B/clk of shared
+// memory per SM at the tensor core's TF32 rate -- all of it -- while N = 256 needs ~92 B/clk, so
+// this orientation reaches the tensor core's rate on the 128-channel layers that dominate the
+// decoder.  TMEM lanes are output channels: an epilogue warp holds 32 channels x 32 time rows,
+// and for each time row its 32 lanes store 32 consecutive channels (one full 128-byte line per
+// warp instruction).  Persistent CTAs walk (128 channels x 256 rows) tiles with two TMEM
+// accumulator sets (2 x 256 columns), channel blocks fastest so consecutive tiles reuse the same
+// activation window from L2.
+constexpr int kTNRows = 256;    // time rows per tile (MMA N)
+constexpr int kTNThreads = 320; // warps 0-7 epilogue, 8 TMA producer, 9 TMEM allocator + MMA
+
+struct TNCfg {
+  static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
+  static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
+  static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
+  static constexpr int kAStages = 8;
+  static constexpr int kBytes = 2 * kWinBytes + kAStages * kA + 1024 + 256;
+};
+
+// Epilogue of one 32-channel x 32-row block: this thread's channel n, time rows t0..t0+31, read
+// from TMEM at `taddr` (D[n][t0 + i] -> column i).  MODE is a compile-time epilogue mode, so each
+// instance carries only its own code.  In the decoder modes the 32 lanes of a warp write 32
+// consecutive channels of one output row per store (a full 128-byte line), inputs of the
+// residual / branch sum are loaded before the TMEM read, and offsets are 32-bit (the decoder
+// keeps every activation tensor below 2^31 elements).
+template <int MODE, int F>
+__device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z, int n, int t0,
+                                       int m_rows, int lane) {
+  const bool has_res = F == EF_GENERIC ? e.res != nullptr : (F & EF_RES) != 0;
+  const int acc_mode = F == EF_GENERIC ? e.acc_mode : (F & EF_ACC2) ? 2 : (F & EF_ACC3) ? 3 : 0;
+  const bool has_out0 = F == EF_GENERIC ? e.out0 != nullptr : (F & EF_OUT0) != 0;
+  const bool has_out1 = F == EF_GENERIC ? e.out1 != nullptr : (F & EF_OUT1) != 0;
+  const bool has_refl = F == EF_GENERIC ? e.refl != 0 : (F & EF_REFL) != 0;
+  if constexpr (MODE == EPI_ROWS || MODE == EPI_ROWS_CONVT) {
+    int col = n, r = 0;
+    if constexpr (MODE == EPI_ROWS_CONVT) {
+      r = n / e.cphase;   // uniform over the warp: a 32-row group never straddles a phase
+      col = n - r * e.cphase;
+    }
+    const int tl = t0 + lane;
+    int my_orow = 0;
+    unsigned char my_mk = 0;
+    if (tl < m_rows) {
+      if constexpr (MODE == EPI_ROWS) {
+        my_orow = tl;
+        my_mk = __ldg(e.mask + tl);
+      } else {
+        const int b = __ldg(e.obase + tl);
+        if (b != INT_MIN) {
+          my_orow = b + e.s * tl + r;
+          my_mk = __ldg(e.mask + my_orow);
+        }
+      }
+    }
+    const unsigned valid = __ballot_sync(0xffffffffu, my_mk & 1);
+    if (!valid) return;   // uniform: no row of this block is stored, skip the TMEM read too
+    const unsigned refl = has_refl ? __ballot_sync(0xffffffffu, (my_mk >> 1) & 1) : 0u;
+    const bool colok = col < e.nstore;
+    const float bias = (e.bias && colok) ? __ldg(e.bias + n) : 0.0f;
+    const int ldc = e.ldc, ldc1 = e.ldc1;
+    // two passes of 16 rows keep the live arrays small (10 warps: <= 168 registers a thread)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const unsigned vh = (valid >> (16 * h)) & 0xffffu, rh = (refl >> (16 * h)) & 0xffffu;
+      if (!vh) continue;   // uniform over the warp
+      const int th = t0 + 16 * h;
+      float rs[16], ac[16];
+      if constexpr (MODE == EPI_ROWS) {
+        const int base = th * ldc + col;
+        if (has_res) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            rs[i] = (((vh >> i) & 1) && colok) ? e.res[base + i * ldc] : 0.0f;
+        }
+        if (acc_mode) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            ac[i] = (((vh >> i) & 1) && colok) ? e.accin[base + i * ldc] : 0.0f;
+        }
+      }
+      float v[16];
+      tmem_ld16(taddr + 16u * h, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        int orow;
+        if constexpr (MODE == EPI_ROWS) orow = th + i;
+        else orow = __shfl_sync(0xffffffffu, my_orow, 16 * h + i);
+        if (!((vh >> i) & 1) || !colok) continue;
+        float x = v[i] + bias;
+        if constexpr (MODE == EPI_ROWS) {
+          if (has_res) x += rs[i];
+          if (acc_mode == 2) x = ac[i] + x;
+          else if (acc_mode == 3) x = (ac[i] + x) / 3.0f;
+        }
+        if (has_out0) e.out0[orow * ldc + col] = x;
+        if (has_out1) {
+          const float w = tf32_rna(leaky(x, e.alpha1));
+          e.out1[orow * ldc1 + col] = w;
+          if (has_refl && ((rh >> i) & 1)) e.out1[(orow - 2) * ldc1 + col] = w;
+        }
+      }
+    }
+  } else {
+    float v[32];
+    tmem_ld32(taddr, v);
+    const float bias = e.bias ? __ldg(e.bias + n) : 0.0f;
+    if constexpr (MODE == EPI_PLAIN_CONV) {
+      if (n >= e.nstore) return;
+      float *y = e.y + (long long)z * e.ybatch;
+      const long long rstride = e.rowmajor ? e.ldy : 1, cstride = e.rowmajor ? 1 : e.ldy;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = t0 + i;
+        if (t < e.tout) {
+          float x = v[i] + bias;
+          if (e.epi0) x = epi_op(x, e.epi0, e.a0);
+          if (e.epi1) x = epi_op(x, e.epi1, e.a1);
+          y[(long long)n * cstride + (long long)t * rstride] = x;
+        }
+      }
+    } else {  // EPI_PLAIN_CONVT
+      if (n >= e.nstore) return;
+      const int r = n / e.cphase, co = n - r * e.cphase;
+      float *y = e.y + (long long)z * e.ybatch + (long long)co * e.ldy;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int t = t0 + i;
+        if (t < m_rows) {
+          const long long oi = (e.q0 + t) * e.s + r - e.pad;
+          if (oi >= 0 && oi < e.tout) {
+            float x = v[i] + bias;
+            if (e.epi0) x = epi_op(x, e.epi0, e.a0);
+            y[oi] = x;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int MODE, int F>
+__global__ void __launch_bounds__(kTNThreads, 1)
+    conv_tc_tn_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                      const ConvGeom g, const EpiParams e, uint32_t *gerr) {
+  using P = TNCfg;
+  constexpr int AS = P::kAStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *gbase = smem_raw + (base - raw);
+  const uint32_t win0 = base, ast0 = base + 2 * P::kWinBytes;
+  const uint32_t bar0 = ast0 + AS * P::kA;
+  auto wfull = [&](int s) { return bar0 + 8u * s; };
+  auto wempty = [&](int s) { return bar0 + 8u * (2 + s); };
+  auto afull = [&](int s) { return bar0 + 8u * (4 + s); };   // accumulator ready
+  auto aempty = [&](int s) { return bar0 + 8u * (6 + s); };  // accumulator drained
+  auto sfull = [&](int s) { return bar0 + 8u * (8 + s); };   // weight stage loaded
+  auto sempty = [&](int s) { return bar0 + 8u * (8 + AS + s); };
+  const uint32_t dbar = bar0 + 8u * (8 + 2 * AS);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (9 + 2 * AS));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kc = g.cin32 / kBK;
+  const int span = (g.ntap - 1) * g.row_step;
+  const int lo_off = span < 0 ? span : 0;
+  const int wrows = kTNRows + (span < 0 ? -span : span);
+  const int nbox = (wrows + kWinBox - 1) / kWinBox;
+  const int mt = (g.n_cols + kBM - 1) / kBM;              // channel tiles (fastest)
+  const int tt = (g.m_rows + kTNRows - 1) / kTNRows;      // time tiles
+  const int ntiles = mt * tt * g.nbatch;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(wfull(s), 1);
+      mbar_init(wempty(s), 1);
+      mbar_init(afull(s), 1);
+      mbar_init(aempty(s), 8);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(sfull(s), 1);
+      mbar_init(sempty(s), 1);
+    }
+    mbar_init(dbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    prefetch_tmap(&tmX);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int wiss[2] = {0, 0}, aiss[AS];
+#pragma unroll
+      for (int s = 0; s < AS; ++s) aiss[s] = 0;
+      bool ok = true;
+      int cw = 0, ca = 0;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int z = t / (mt * tt), r = t - z * mt * tt, ti = r / mt, mi = r - ti * mt;
+        const int wlo = ti * kTNRows + g.row_off0 + lo_off;
+        for (int c = 0; c < kc && ok; ++c, ++cw) {
+          const int ws = cw & 1;
+          if (!mbar_wait(wempty(ws), ((cw >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t wb = win0 + ws * P::kWinBytes;
+          mbar_expect_tx(wfull(ws), nbox * kWinBox * kBK * 4);
+          for (int b = 0; b < nbox; ++b)
+            tma_load_3d(wb + b * kWinBox * kBK * 4, &tmX, wfull(ws), c * kBK, wlo + b * kWinBox, z);
+          ++wiss[ws];
+          for (int k = 0; k < g.ntap; ++k, ++ca) {
+            const int as = ca % AS;
+            if (!mbar_wait(sempty(as), ((ca / AS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(sfull(as), P::kA);
+            tma_load_2d(ast0 + as * P::kA, &tmW, sfull(as), k * g.cin32 + c * kBK, mi * kBM);
+            ++aiss[as];
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < 2; ++s)
+          if (wiss[s]) {
+            uint32_t it = 0;
+            while (!mbar_try_wait(wfull(s), (wiss[s] - 1) & 1) && ++it < kWaitLimit) {
+            }
+            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+          }
+        for (int s = 0; s < AS; ++s)
+          if (aiss[s]) {
+            uint32_t it = 0;
+            while (!mbar_try_wait(sfull(s), (aiss[s] - 1) & 1) && ++it < kWaitLimit) {
+            }
+            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+          }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------- MMA issuer: M = 128 channels, N = 256 time rows
+      const uint32_t idesc = idesc_tf32(kBM, kTNRows);
+      bool ok = true;
+      int cw = 0, ca = 0, it = 0;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+        const int ab = it & 1;
+        if (!mbar_wait(aempty(ab), ((it >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + ab * kTNRows;
+        for (int c = 0; c < kc && ok; ++c, ++cw) {
+          const int ws = cw & 1;
+          if (!mbar_wait(wfull(ws), (cw >> 1) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+            ok = false;
+            break;
+          }
+          const uint32_t wb = win0 + ws * P::kWinBytes;
+          for (int k = 0; k < g.ntap; ++k, ++ca) {
+            const int as = ca % AS;
+            if (!mbar_wait(sfull(as), (ca / AS) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t da = sdesc_kmajor_sw128(ast0 + as * P::kA);
+            const uint64_t db =
+                sdesc_kmajor_sw128(wb + (uint32_t)(k * g.row_step - lo_off) * (kBK * 4));
+#pragma unroll
+            for (int kk = 0; kk < kBK / 8; ++kk)
+              mma_tf32(acc, da + 2u * kk, db + 2u * kk, idesc, (c | k | kk) != 0);
+            mma_commit(sempty(as));
+          }
+          if (ok) mma_commit(wempty(ws));
+        }
+        if (ok) mma_commit(afull(ab));
+      }
+      if (!ok) {
+        mma_commit(dbar);
+        uint32_t n = 0;
+        while (!mbar_try_wait(dbar, 0) && ++n < kWaitLimit) {
+        }
+        if (n >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 0..7: lane quarter (channels) x time half
+    const int q = warp & 3, half = warp >> 2;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int ab = it & 1;
+      if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
+      tc_fence_after();
+      const int z = t / (mt * tt), r = t - z * mt * tt, ti = r / mt, mi = r - ti * mt;
+      const int co_row = mi * kBM + q * 32 + lane;
+      const uint32_t tl = tmem + ab * kTNRows + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int j = half * 4; j < half * 4 + 4; ++j)
+        tn_epi<MODE, F>(e, tl + 32u * j, z, co_row, ti * kTNRows + 32 * j, g.m_rows, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(aempty(ab));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+#endif  // PTB_CONV_KERNELS
 
 }  // namespace ptb

@@ -153,7 +153,10 @@ int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
     p.total_z += 192 * T[i];
     p.total_wav += 256 * T[i];
   }
-  PTB_REQUIRE(p.R[2] < (int64_t)INT_MAX / 2, "pt_b200: batch too large (%lld level-2 rows)",
+  // epilogue offsets are 32-bit: every activation tensor must stay below 2^31 elements
+  PTB_REQUIRE(p.R[2] * 128 < (int64_t)INT_MAX && p.R[0] * 512 < (int64_t)INT_MAX &&
+                  p.R[1] * 256 < (int64_t)INT_MAX,
+              "pt_b200: batch too large (%lld level-2 rows); split it into smaller batches",
               (long long)p.R[2]);
   // host tables in one pinned block
   std::vector<unsigned char> m[3], mr, mp;
@@ -379,6 +382,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
               e.out1 = d->P;
               e.alpha1 = kLrFinal;
               e.mask = p.mask_refl;
+              e.refl = 1;
             }
           }
           if (run_conv(d, st, d->rb2[r][j], d->H[s], rout, -(K - 1) / 2, 1, e)) return -1;
