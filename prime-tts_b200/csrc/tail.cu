@@ -19,12 +19,24 @@
 
 namespace ptb {
 
-constexpr int kTailW = 1024;                 // output samples per CTA
+constexpr int kTailW = 1024;                 // output samples per CTA (static smem < 48 KiB)
 constexpr int kTailThreads = 256;
-constexpr int kTailF = kTailW / 16 + 12;     // staged frames (chunk + halo)
+constexpr int kTailF = kTailW / 16 + 8;      // staged frames (chunk + halo): NF <= W/16 + 5
 constexpr int kTailM = kTailW / 4 + 20;      // staged trimmed-OLA samples per band
 
 __constant__ float c_bc[144], c_bs[144], c_win[16], c_win2[16];
+__constant__ double c_bcd[144], c_bsd[144];   // the same bases, exact in double
+
+// Frame rows are 68 floats (4 bands x 16 + 4 pad): the overlap-add reads 8 consecutive frames at
+// one (band, sample) per warp and the stride of 68 puts those reads on 32 distinct banks.
+constexpr int kFrStride = 68;
+struct TailSmem {
+  double re[kTailF][4][9], im[kTailF][4][9];   // per frame, band, bin (converted once)
+  float fr[kTailF][kFrStride];                 // windowed frames, [frame][band * 16 + n]
+  float4 sm[kTailM];                           // trimmed OLA, 4 bands interleaved
+  float4 h[63];                                // PQMF taps, 4 bands interleaved
+  float win2[16];
+};
 
 struct TailArgs {
   const float *post;      // element (channel c, frame f) of request r:
@@ -42,9 +54,12 @@ __device__ __forceinline__ float tr_sin(float x, bool f32) { return f32 ? sinf(x
 __device__ __forceinline__ float tr_cos(float x, bool f32) { return f32 ? cosf(x) : (float)cos((double)x); }
 
 __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
-  __shared__ float fr[4][kTailF][16];
-  __shared__ float sm[4][kTailM];
-  __shared__ float h[4][63];
+  extern __shared__ __align__(16) unsigned char tail_smem[];
+  TailSmem &S = *reinterpret_cast<TailSmem *>(tail_smem);
+  auto &re = S.re;
+  auto &im = S.im;
+  auto &fr = S.fr;
+  auto &sm = S.sm;
   const int req = blockIdx.y;
   const long long Tp = a.tp ? a.tp[req] : a.tp1;
   const long long nwav = 16 * (Tp - 1);
@@ -55,7 +70,19 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   // the reference switches Exp/Sin/Cos to fp32 libm only for tensors of >= 4096 elements
   const bool f32 = 36 * Tp >= 4096;
 
-  for (int i = threadIdx.x; i < 4 * 63; i += blockDim.x) h[i / 63][i % 63] = a.pqmf[i];
+  float *hf = reinterpret_cast<float *>(S.h);
+  for (int i = threadIdx.x; i < 4 * 63; i += blockDim.x) hf[(i % 63) * 4 + i / 63] = a.pqmf[i];
+  if (threadIdx.x < 16) S.win2[threadIdx.x] = c_win2[threadIdx.x];
+  // the output bin n of phase 1b is fixed per thread (the block size is a multiple of 16), so its
+  // basis column and window value live in registers
+  const int n = threadIdx.x & 15;
+  double bcn[9], bsn[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    bcn[k] = c_bcd[k * 16 + n];
+    bsn[k] = c_bsd[k * 16 + n];
+  }
+  const float wn = c_win[n];
 
   // trimmed-OLA samples m needed by outputs [j0, j0 + W): stuffed index 4m in [j - 31, j + 31]
   long long m_lo = (j0 - 31 + 3) >> 2;
@@ -66,80 +93,82 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   const long long F0 = ((m_lo + 8) >> 2) - 3;
   const int NF = (int)(((m_hi + 8) >> 2) - F0 + 1);
 
-  // ---- 1. frames
-  for (int it = threadIdx.x; it < 4 * NF; it += blockDim.x) {
-    const int b = it / NF, fl = it - b * NF;
+  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im
+  for (int it = threadIdx.x; it < NF * 36; it += blockDim.x) {
+    const int fl = it / 36, rb = it - fl * 36, b = rb / 9, k = rb - b * 9;
     const long long f = F0 + fl;
-    float out[16];
+    float rv = 0.0f, iv = 0.0f;   // frames outside [0, Tp) never reach the overlap-add
     if (f >= 0 && f < Tp) {
-      float re[9], im[9];
       const float *pf = post + f * a.st_t;
-#pragma unroll
-      for (int k = 0; k < 9; ++k) {
-        const float mag = tr_exp(pf[(long long)(b * 18 + k) * a.st_c], f32);
-        const float ph = __fmul_rn(tr_sin(pf[(long long)(b * 18 + 9 + k) * a.st_c], f32),
-                                   3.1415927410125732f);
-        re[k] = __fmul_rn(mag, tr_cos(ph, f32));
-        im[k] = __fmul_rn(mag, tr_sin(ph, f32));
-      }
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        double er = 0.0, ei = 0.0;
-#pragma unroll
-        for (int k = 0; k < 9; ++k) {
-          const float bc = c_bc[k * 16 + n], bs = c_bs[k * 16 + n];
-          if (bc != 0.0f) er = __dadd_rn(er, __dmul_rn((double)bc, (double)re[k]));
-          if (bs != 0.0f) ei = __dadd_rn(ei, __dmul_rn((double)bs, (double)im[k]));
-        }
-        out[n] = __fmul_rn(__fadd_rn((float)er, (float)ei), c_win[n]);
-      }
-    } else {
-#pragma unroll
-      for (int n = 0; n < 16; ++n) out[n] = 0.0f;
+      const float mag = tr_exp(pf[(long long)(b * 18 + k) * a.st_c], f32);
+      const float ph = __fmul_rn(tr_sin(pf[(long long)(b * 18 + 9 + k) * a.st_c], f32),
+                                 3.1415927410125732f);
+      rv = __fmul_rn(mag, tr_cos(ph, f32));
+      iv = __fmul_rn(mag, tr_sin(ph, f32));
     }
+    re[fl][b][k] = (double)rv;
+    im[fl][b][k] = (double)iv;
+  }
+  __syncthreads();
+  // ---- 1b. per (frame, band, output bin): the 9 -> 16 basis sums in double, then the window
+  static_assert(kTailThreads % 16 == 0, "phase 1b keeps n = threadIdx.x % 16");
+  for (int it = threadIdx.x; it < NF * 64; it += blockDim.x) {
+    const int fl = it >> 6, b = (it >> 4) & 3;
+    double er = 0.0, ei = 0.0;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) fr[b][fl][n] = out[n];
+    for (int k = 0; k < 9; ++k) {   // zero basis entries are skipped, as in the reference einsum
+      if (bcn[k] != 0.0) er = __dadd_rn(er, __dmul_rn(bcn[k], re[fl][b][k]));
+      if (bsn[k] != 0.0) ei = __dadd_rn(ei, __dmul_rn(bsn[k], im[fl][b][k]));
+    }
+    fr[fl][b * 16 + n] = __fmul_rn(__fadd_rn((float)er, (float)ei), wn);
   }
   __syncthreads();
 
-  // ---- 2. overlap-add / window-sum envelope, trimmed [8:-8]
+  // ---- 2. overlap-add / window-sum envelope, trimmed [8:-8]; frames outside [0, Tp) are absent
   const int NM = (int)(m_hi - m_lo + 1);
-  for (int it = threadIdx.x; it < 4 * NM; it += blockDim.x) {
-    const int b = it / NM, ml = it - b * NM;
+  for (int ml = threadIdx.x; ml < NM; ml += blockDim.x) {
     const long long p = m_lo + ml + 8;
     const long long q = p >> 2;
     const int r = (int)(p & 3);
-    float ola = 0.0f, env = 0.0f;
+    float ola[4] = {0.0f, 0.0f, 0.0f, 0.0f}, env = 0.0f;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const long long qq = q - t;
       if (qq >= 0 && qq < Tp) {
-        ola = __fadd_rn(ola, fr[b][qq - F0][r + 4 * t]);
-        env = __fadd_rn(env, c_win2[r + 4 * t]);
+        const int fl = (int)(qq - F0);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) ola[b] = __fadd_rn(ola[b], fr[fl][b * 16 + r + 4 * t]);
+        env = __fadd_rn(env, S.win2[r + 4 * t]);
       }
     }
     const float ec = env > 1e-9f ? env : 1e-9f;
-    sm[b][ml] = __fdiv_rn(ola, ec);
+    sm[ml] = make_float4(__fdiv_rn(ola[0], ec), __fdiv_rn(ola[1], ec), __fdiv_rn(ola[2], ec),
+                         __fdiv_rn(ola[3], ec));
   }
   __syncthreads();
 
   // ---- 3. x4 zero-stuff (gain 4) + 63-tap PQMF synthesis, tap-major then band (conv order)
   float *wav = a.wav + (a.wav0 ? a.wav0[req] : 0);
-  for (int jj = threadIdx.x; jj < kTailW; jj += blockDim.x) {
-    const long long j = j0 + jj;
-    if (j >= nwav) break;
+  const int jn = (int)(nwav - j0 < kTailW ? nwav - j0 : kTailW);
+  const int mlo = (int)m_lo, nw = (int)nwav, jb = (int)j0;
+  for (int jj = threadIdx.x; jj < jn; jj += blockDim.x) {
+    const int j = jb + jj;
     float acc = 0.0f;
-    const int k0 = (int)((31 - j) & 3);  // first tap with (j + k - 31) % 4 == 0
+    const int k0 = (31 - j) & 3;  // first tap with (j + k - 31) % 4 == 0
+#pragma unroll 4
     for (int k = k0; k < 63; k += 4) {
-      const long long i = j + k - 31;
-      if (i < 0 || i >= nwav) continue;
-      const int ml = (int)((i >> 2) - m_lo);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const float x = __fmul_rn(4.0f, sm[b][ml]);
-        if (x == 0.0f) continue;
-        acc = __fadd_rn(acc, __fmul_rn(h[b][k], x));
-      }
+      const int i = j + k - 31;
+      if (i < 0 || i >= nw) continue;
+      const float4 s4 = sm[(i >> 2) - mlo];
+      const float4 h4 = S.h[k];
+      float x = __fmul_rn(4.0f, s4.x);
+      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.x, x));
+      x = __fmul_rn(4.0f, s4.y);
+      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.y, x));
+      x = __fmul_rn(4.0f, s4.z);
+      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.z, x));
+      x = __fmul_rn(4.0f, s4.w);
+      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.w, x));
     }
     wav[j] = acc;
   }
@@ -169,7 +198,14 @@ static void tail_constants_init() {
       bs[k * 16 + n] = p2 / 16.0f;
     }
   }
-  if (cudaMemcpyToSymbol(c_bc, bc, sizeof(bc)) != cudaSuccess ||
+  double bcd[144], bsd[144];
+  for (int i = 0; i < 144; ++i) {
+    bcd[i] = (double)bc[i];
+    bsd[i] = (double)bs[i];
+  }
+  if (cudaMemcpyToSymbol(c_bcd, bcd, sizeof(bcd)) != cudaSuccess ||
+      cudaMemcpyToSymbol(c_bsd, bsd, sizeof(bsd)) != cudaSuccess ||
+      cudaMemcpyToSymbol(c_bc, bc, sizeof(bc)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_bs, bs, sizeof(bs)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win, win, sizeof(win)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win2, win2, sizeof(win2)) != cudaSuccess)
@@ -188,6 +224,8 @@ static int tail_ready() {
     g_tail_err = 0;
     tail_constants_init();
     PTB_REQUIRE(!g_tail_err, "pt_b200: tail constant upload failed");
+    PTB_CUDA(cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(TailSmem)));
     done[dev] = true;
   }
   return 0;
@@ -206,7 +244,7 @@ int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wa
   a.wav = wav_dev;
   const long long nwav = 16 * (Tp - 1);
   dim3 grid((unsigned)((nwav + kTailW - 1) / kTailW), 1);
-  tail_kernel<<<grid, kTailThreads, 0, st>>>(a);
+  tail_kernel<<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;
@@ -228,7 +266,7 @@ int tail_run_rows(const float *post_dev, long long ld, const long long *row0, co
   a.wav = wav_dev;
   const long long nwav = 16 * (max_tp - 1);
   dim3 grid((unsigned)((nwav + kTailW - 1) / kTailW), (unsigned)nreq);
-  tail_kernel<<<grid, kTailThreads, 0, st>>>(a);
+  tail_kernel<<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;
