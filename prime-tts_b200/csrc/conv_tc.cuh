@@ -893,90 +893,12 @@ struct TNCfg {
   static constexpr int kBytes = 2 * kWinBytes + kAStages * kA + 1024 + 256;
 };
 
-// Epilogue of one 32-channel x 32-row block: this thread's channel n, time rows t0..t0+31, read
-// from TMEM at `taddr` (D[n][t0 + i] -> column i).  MODE is a compile-time epilogue mode, so each
-// instance carries only its own code.  In the decoder modes the 32 lanes of a warp write 32
-// consecutive channels of one output row per store (a full 128-byte line), inputs of the
-// residual / branch sum are loaded before the TMEM read, and offsets are 32-bit (the decoder
-// keeps every activation tensor below 2^31 elements).
+// Plain-mode (interpreter ABI) epilogue of one 32-channel x 32-row block: this thread's channel
+// n, time rows t0..t0+31, read from TMEM at `taddr` (D[n][t0 + i] -> column i).
 template <int MODE, int F>
 __device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z, int n, int t0,
-                                       int m_rows, int lane) {
-  const bool has_res = F == EF_GENERIC ? e.res != nullptr : (F & EF_RES) != 0;
-  const int acc_mode = F == EF_GENERIC ? e.acc_mode : (F & EF_ACC2) ? 2 : (F & EF_ACC3) ? 3 : 0;
-  const bool has_out0 = F == EF_GENERIC ? e.out0 != nullptr : (F & EF_OUT0) != 0;
-  const bool has_out1 = F == EF_GENERIC ? e.out1 != nullptr : (F & EF_OUT1) != 0;
-  const bool has_refl = F == EF_GENERIC ? e.refl != 0 : (F & EF_REFL) != 0;
-  if constexpr (MODE == EPI_ROWS || MODE == EPI_ROWS_CONVT) {
-    int col = n, r = 0;
-    if constexpr (MODE == EPI_ROWS_CONVT) {
-      r = n / e.cphase;   // uniform over the warp: a 32-row group never straddles a phase
-      col = n - r * e.cphase;
-    }
-    const int tl = t0 + lane;
-    int my_orow = 0;
-    unsigned char my_mk = 0;
-    if (tl < m_rows) {
-      if constexpr (MODE == EPI_ROWS) {
-        my_orow = tl;
-        my_mk = __ldg(e.mask + tl);
-      } else {
-        const int b = __ldg(e.obase + tl);
-        if (b != INT_MIN) {
-          my_orow = b + e.s * tl + r;
-          my_mk = __ldg(e.mask + my_orow);
-        }
-      }
-    }
-    const unsigned valid = __ballot_sync(0xffffffffu, my_mk & 1);
-    if (!valid) return;   // uniform: no row of this block is stored, skip the TMEM read too
-    const unsigned refl = has_refl ? __ballot_sync(0xffffffffu, (my_mk >> 1) & 1) : 0u;
-    const bool colok = col < e.nstore;
-    const float bias = (e.bias && colok) ? __ldg(e.bias + n) : 0.0f;
-    const int ldc = e.ldc, ldc1 = e.ldc1;
-    // two passes of 16 rows keep the live arrays small (10 warps: <= 168 registers a thread)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const unsigned vh = (valid >> (16 * h)) & 0xffffu, rh = (refl >> (16 * h)) & 0xffffu;
-      if (!vh) continue;   // uniform over the warp
-      const int th = t0 + 16 * h;
-      float rs[16], ac[16];
-      if constexpr (MODE == EPI_ROWS) {
-        const int base = th * ldc + col;
-        if (has_res) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            rs[i] = (((vh >> i) & 1) && colok) ? e.res[base + i * ldc] : 0.0f;
-        }
-        if (acc_mode) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            ac[i] = (((vh >> i) & 1) && colok) ? e.accin[base + i * ldc] : 0.0f;
-        }
-      }
-      float v[16];
-      tmem_ld16(taddr + 16u * h, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        int orow;
-        if constexpr (MODE == EPI_ROWS) orow = th + i;
-        else orow = __shfl_sync(0xffffffffu, my_orow, 16 * h + i);
-        if (!((vh >> i) & 1) || !colok) continue;
-        float x = v[i] + bias;
-        if constexpr (MODE == EPI_ROWS) {
-          if (has_res) x += rs[i];
-          if (acc_mode == 2) x = ac[i] + x;
-          else if (acc_mode == 3) x = (ac[i] + x) / 3.0f;
-        }
-        if (has_out0) e.out0[orow * ldc + col] = x;
-        if (has_out1) {
-          const float w = tf32_rna(leaky(x, e.alpha1));
-          e.out1[orow * ldc1 + col] = w;
-          if (has_refl && ((rh >> i) & 1)) e.out1[(orow - 2) * ldc1 + col] = w;
-        }
-      }
-    }
-  } else {
+                                       int m_rows) {
+  if constexpr (MODE == EPI_PLAIN_CONV || MODE == EPI_PLAIN_CONVT) {
     float v[32];
     tmem_ld32(taddr, v);
     const float bias = e.bias ? __ldg(e.bias + n) : 0.0f;
@@ -1010,6 +932,91 @@ __device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z
           }
         }
       }
+    }
+  }
+}
+
+// Rows-mode (decoder) epilogue.  An epilogue warp owns 32 channels (its TMEM lane quarter) x 128
+// time rows of a tile: four 32-row blocks of two 16-row passes.  Everything that does not depend on
+// the accumulator -- the per-row output map and masks of all four blocks, the bias, and the first
+// pass's residual / branch-sum inputs -- is loaded before the accumulator wait, and each pass's
+// inputs are requested one pass ahead of their use, so a warp keeps loads in flight instead of
+// waiting on one dependent round trip per block.  Residual and branch-sum rows below m_rows are
+// always inside their (m_rows x ldc) buffers, so these loads need no mask.
+template <int MODE, int F>
+struct TNRowsFlags {
+  __device__ __forceinline__ static bool res(const EpiParams &e) {
+    return F == EF_GENERIC ? e.res != nullptr : (F & EF_RES) != 0;
+  }
+  __device__ __forceinline__ static int acc(const EpiParams &e) {
+    return F == EF_GENERIC ? e.acc_mode : (F & EF_ACC2) ? 2 : (F & EF_ACC3) ? 3 : 0;
+  }
+  __device__ __forceinline__ static bool out0(const EpiParams &e) {
+    return F == EF_GENERIC ? e.out0 != nullptr : (F & EF_OUT0) != 0;
+  }
+  __device__ __forceinline__ static bool out1(const EpiParams &e) {
+    return F == EF_GENERIC ? e.out1 != nullptr : (F & EF_OUT1) != 0;
+  }
+  __device__ __forceinline__ static bool refl(const EpiParams &e) {
+    return F == EF_GENERIC ? e.refl != 0 : (F & EF_REFL) != 0;
+  }
+};
+
+// residual / branch-sum inputs of rows th .. th+15 for this lane's output column
+template <int MODE, int F>
+__device__ __forceinline__ void tn_rows_load(const EpiParams &e, int th, int col, bool colok,
+                                             int m_rows, float (&rs)[16], float (&ac)[16]) {
+  using FL = TNRowsFlags<MODE, F>;
+  if constexpr (MODE == EPI_ROWS) {
+    const bool hr = FL::res(e);
+    const int am = FL::acc(e);
+    if (!hr && !am) return;
+    const int ldc = e.ldc, base = th * ldc + col;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const bool ok = colok && th + i < m_rows;
+      if (hr) rs[i] = ok ? e.res[base + i * ldc] : 0.0f;
+      if (am) ac[i] = ok ? e.accin[base + i * ldc] : 0.0f;
+    }
+  }
+}
+
+// One 16-row pass: rows th .. th+15 are TMEM columns taddr .. taddr+15.  `mk` is this lane's row
+// mask in the pass's 32-row block (bit 0 store, bit 1 also store the reflected row) and
+// `orow_blk` its output row (row-map mode).
+template <int MODE, int F>
+__device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr, int th, int h,
+                                             int col, bool colok, float bias, unsigned mk,
+                                             int orow_blk, const float (&rs)[16],
+                                             const float (&ac)[16]) {
+  using FL = TNRowsFlags<MODE, F>;
+  const bool hr = FL::res(e), o0 = FL::out0(e), o1 = FL::out1(e), hrefl = FL::refl(e);
+  const int am = FL::acc(e);
+  const unsigned valid = __ballot_sync(0xffffffffu, mk & 1u);
+  const unsigned vh = (valid >> (16 * h)) & 0xffffu;
+  if (!vh) return;   // uniform over the warp: nothing of this pass is stored
+  const unsigned rh =
+      hrefl ? (__ballot_sync(0xffffffffu, (mk >> 1) & 1u) >> (16 * h)) & 0xffffu : 0u;
+  const int ldc = e.ldc, ldc1 = e.ldc1;
+  float v[16];
+  tmem_ld16(taddr, v);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    int orow;
+    if constexpr (MODE == EPI_ROWS) orow = th + i;
+    else orow = __shfl_sync(0xffffffffu, orow_blk, 16 * h + i);
+    if (!((vh >> i) & 1) || !colok) continue;
+    float x = v[i] + bias;
+    if constexpr (MODE == EPI_ROWS) {
+      if (hr) x += rs[i];
+      if (am == 2) x = ac[i] + x;
+      else if (am == 3) x = (ac[i] + x) / 3.0f;
+    }
+    if (o0) e.out0[orow * ldc + col] = x;
+    if (o1) {
+      const float w = tf32_rna(leaky(x, e.alpha1));
+      e.out1[orow * ldc1 + col] = w;
+      if (hrefl && ((rh >> i) & 1)) e.out1[(orow - 2) * ldc1 + col] = w;
     }
   }
 }
@@ -1179,14 +1186,61 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int ab = it & 1;
-      if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
-      tc_fence_after();
       const int z = t / (mt * tt), r = t - z * mt * tt, ti = r / mt, mi = r - ti * mt;
       const int co_row = mi * kBM + q * 32 + lane;
       const uint32_t tl = tmem + ab * kTNRows + (static_cast<uint32_t>(q * 32) << 16);
+      if constexpr (MODE == EPI_ROWS || MODE == EPI_ROWS_CONVT) {
+        int col = co_row, ph = 0;
+        if constexpr (MODE == EPI_ROWS_CONVT) {
+          ph = co_row / e.cphase;   // uniform over the warp: 32 lanes never straddle a phase
+          col = co_row - ph * e.cphase;
+        }
+        const bool colok = col < e.nstore;
+        const float bias = (e.bias && colok) ? __ldg(e.bias + co_row) : 0.0f;
+        const int rb = ti * kTNRows + half * 128;   // this warp's first time row
+        // output row map and masks of the four blocks (lane = row within the block)
+        int orow[4];
+        unsigned mk = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int tr = rb + 32 * j + lane;
+          orow[j] = -1;
+          if (tr < g.m_rows) {
+            if constexpr (MODE == EPI_ROWS) {
+              orow[j] = tr;
+            } else {
+              const int b = __ldg(e.obase + tr);
+              if (b != INT_MIN) orow[j] = b + e.s * tr + ph;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (orow[j] >= 0) mk |= static_cast<unsigned>(__ldg(e.mask + orow[j])) << (8 * j);
+        float rsA[16], acA[16];
+        tn_rows_load<MODE, F>(e, rb, col, colok, g.m_rows, rsA, acA);
+        if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
+        tc_fence_after();
+        const uint32_t tw = tl + static_cast<uint32_t>(half * 128);
 #pragma unroll 1
-      for (int j = half * 4; j < half * 4 + 4; ++j)
-        tn_epi<MODE, F>(e, tl + 32u * j, z, co_row, ti * kTNRows + 32 * j, g.m_rows, lane);
+        for (int j = 0; j < 4; ++j) {
+          const int th = rb + 32 * j;
+          const unsigned mj = (mk >> (8 * j)) & 0xffu;
+          const int oj = j == 0 ? orow[0] : j == 1 ? orow[1] : j == 2 ? orow[2] : orow[3];
+          float rsB[16], acB[16];
+          tn_rows_load<MODE, F>(e, th + 16, col, colok, g.m_rows, rsB, acB);
+          tn_rows_pass<MODE, F>(e, tw + 32u * j, th, 0, col, colok, bias, mj, oj, rsA, acA);
+          if (j < 3) tn_rows_load<MODE, F>(e, th + 32, col, colok, g.m_rows, rsA, acA);
+          tn_rows_pass<MODE, F>(e, tw + 32u * j + 16u, th + 16, 1, col, colok, bias, mj, oj, rsB,
+                                acB);
+        }
+      } else {
+        if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int j = half * 4; j < half * 4 + 4; ++j)
+          tn_epi<MODE, F>(e, tl + 32u * j, z, co_row, ti * kTNRows + 32 * j, g.m_rows);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(aempty(ab));
