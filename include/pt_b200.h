@@ -254,6 +254,47 @@ PT_B200_API int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double
  * z [192][T] host -> wav [256*T] host. */
 PT_B200_API int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav);
 
+/* ---- Streaming (extension) ------------------------------------------------------------------
+ * The reference streams the decoder on sliding windows of one utterance's frames
+ * (pt_v21_stream_open / _chunk / _close, runtime/v21/src/pt_v21_host.c:2749-2912: each chunk
+ * re-runs the decoder nodes on frames [a, a+win)) and its drivers stitch the window interiors
+ * (main_v21.c:331-368, main_v21_serve.c:210-264).  Here a window is one request of the batched
+ * decoder, and the tail kernel writes each window's interior straight into the stitched output.
+ *
+ * One window: decode latent frames z_dev[z_off + c*z_ld + t] (c < 192, t < frames: a column
+ * slice of a [192][z_ld] latent) as one request, and write its output samples
+ * [keep_lo, keep_hi) (0 <= keep_lo < keep_hi <= 256*frames) to wav_dev[dst + (j - keep_lo)]. */
+typedef struct {
+  int64_t frames, z_off, z_ld, keep_lo, keep_hi, dst;
+} pt_b200_window;
+
+/* Decode n windows in one device-resident pass (asynchronous on `stream`, like
+ * pt_b200_decode_batch_device; pt_b200_decoder_sync reports device errors). */
+PT_B200_API int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n,
+                                       const pt_b200_window *w, const float *z_dev, float *wav_dev);
+
+/* The window plan for nstreams utterances of T[i] frames (latents concatenated as [192][T[i]]
+ * blocks, stitched waveforms as [256*T[i]] blocks), step = max(1, win - 2*ctx):
+ *  exact = 0  the reference's overlap-save (main_v21.c:342-364): windows [a, a+win) every `step`
+ *             frames; the first emits from its start, the last to its end, the others frames
+ *             [a+ctx, a+win-ctx).  Samples near a window edge see zero padding instead of the
+ *             neighbouring frames, so the stitched waveform differs from a whole-utterance decode.
+ *  exact = 1  the same emission schedule (frames [e, e+step) per window), each window decoded
+ *             over [e - max(ctx,25), e + step + max(ctx,24)) clipped to the utterance: the
+ *             decoder's receptive radius is 25 frames back and 24 ahead, so every emitted sample
+ *             equals the whole-utterance decode.
+ * Writes min(cap, count) windows to `out` and returns the window count (cap 0 sizes), -1 on
+ * bad arguments. */
+PT_B200_API int64_t pt_b200_stream_plan(int nstreams, const int64_t *T, int win, int ctx,
+                                        int exact, pt_b200_window *out, int64_t cap);
+
+/* Plan, decode and stitch every stream: windows in plan order, max_frames latent frames per
+ * decode pass (<= 0: 65536).  Device buffers; asynchronous on `stream` except that each new
+ * batch waits for the previous one (they share the decoder's activation buffers). */
+PT_B200_API int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstreams,
+                                      const int64_t *T, const float *z_dev, int win, int ctx,
+                                      int exact, int64_t max_frames, float *wav_dev);
+
 /* Conv1d with no device allocation (no counterpart in the reference).  For callers that cannot
  * call cudaMalloc/cudaFree: hosts that own every device allocation (pooled or framework
  * allocators), real-time threads that must not take the allocator's locks, processes whose

@@ -146,6 +146,43 @@ class CpuDecoder:
         return wav
 
 
+def overlap_save_windows(T: int, win: int, ctx: int, hop: int = 256) -> list:
+    """The reference's overlap-save stitch loop (runtime/v21/src/main_v21.c:342-364) for one
+    utterance of T frames: [(a, win_eff, lo, hi)] -- window frames [a, a+win_eff), whose output
+    samples [lo, hi) are appended to the stitched waveform in order."""
+    out = []
+    step = win - 2 * ctx
+    if step < 1:
+        step = 1
+    a = 0
+    while True:
+        win_eff = win
+        if a + win_eff > T:
+            win_eff = T - a
+        first, last = a == 0, a + win_eff >= T
+        n = win_eff * hop
+        lo = 0 if first else ctx * hop
+        hi = n if last else (win_eff - ctx) * hop
+        if hi > n:
+            hi = n
+        if hi > lo:
+            out.append((a, win_eff, lo, hi))
+        if last:
+            break
+        a += step
+    return out
+
+
+def stitch(decode, z: np.ndarray, windows: list) -> np.ndarray:
+    """Decode each window's frames with ``decode(z_slice) -> wav`` and concatenate the kept
+    samples, as the reference driver does with pt_v21_stream_chunk (main_v21.c:346-360)."""
+    parts = []
+    for a, we, lo, hi in windows:
+        wav = decode(np.ascontiguousarray(z[:, a:a + we]))
+        parts.append(wav[lo:hi])
+    return np.concatenate(parts)
+
+
 def metrics(est: np.ndarray, ref: np.ndarray) -> dict:
     """The reference's parity metrics (tests/v21_reference.py:430-447): max|a-b|/max|b| and
     SNDR = 10 log10(sum ref^2 / sum (est-ref)^2)."""

@@ -2,10 +2,16 @@
 //
 // Ragged batch layout.  At each time resolution (level 0: latent frames T, level 1: 4T after
 // ups.0, level 2: 16T after ups.1) the requests are stacked along time in one channels-last
-// tensor [rows][C], each request's rows preceded and followed by kGap zero rows.  kGap (32)
-// exceeds every conv's reach (dilation 5 x (11-1)/2 = 25 rows), so one launch per layer computes
-// every request exactly as if it ran alone: the zero gap rows are the convolutions' zero padding,
-// and the epilogue never writes them (a per-row mask), so they stay zero.
+// tensor [rows][C], each request's rows preceded and followed by zero gap rows: kGap[0] = 8 at
+// level 0 (conv_pre reaches 3 rows, ups.0 reads 2 before and 1 after a request) and kGap[1..2] = 28
+// at levels 1 and 2 (the widest conv reaches dilation 5 x (11-1)/2 = 25 rows; conv_post reads
+// 3 + 1 reflection row).  So one launch per layer computes every request exactly as if it ran
+// alone: the zero gap rows are the convolutions' zero padding, and the epilogue never writes them
+// (a per-row mask), so they stay zero.
+//
+// A request is a window (pt_b200_window): a column slice of a latent (offset, channel stride),
+// the output samples it keeps and where they go.  Whole utterances keep everything; streaming
+// windows keep their interiors, which the tail kernel writes straight into the stitched output.
 //
 // Graph wiring (ref/v21_graph_trace.txt 3819-4065), with every elementwise node fused:
 //   conv_pre(+LeakyRelu) -> ups.0 (writes u and leaky(u)) ->
@@ -23,15 +29,20 @@
 
 namespace ptb {
 int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
-                  const long long *wav0, int nreq, long long max_tp, const float *pqmf_dev,
-                  float *wav_dev, cudaStream_t st);
+                  const long long *wav0, const long long *klo, const long long *khi, int nreq,
+                  long long max_tp, const float *pqmf_dev, float *wav_dev, cudaStream_t st);
 }  // namespace ptb
 
 using namespace ptb;
 
 namespace {
 
-constexpr int kGap = 32;
+constexpr int64_t kGap[3] = {8, 28, 28};
+// receptive radius of one output sample, in latent frames before / after its own frame
+// (PQMF 63 taps, overlap-add, conv_post k7, two MRF blocks reaching 60 rows, two k16/s4 convT,
+// conv_pre k7, propagated back to the latent)
+constexpr int64_t kReachLeft = 25, kReachRight = 24;
+constexpr int64_t kStreamBatchFrames = 65536;   // default latent frames per streaming batch
 constexpr int kK[3] = {3, 7, 11};
 constexpr int kD[3] = {1, 3, 5};
 constexpr float kLr = 0.10000000149011612f;
@@ -64,10 +75,11 @@ int make_layer(DLayer *L, const float *wp, const float *bias, int rows4, int nta
   return 0;
 }
 
-// scatter the concatenated channel-major latents [192][T_i] into the level-0 rows, tf32-rounded
+// scatter each request's channel-major latent columns (z[zoff + c*zld + t], t < T) into the
+// level-0 rows, tf32-rounded
 __global__ void stage_z_kernel(const float *__restrict__ z, const long long *__restrict__ zoff,
-                               const long long *__restrict__ T, const long long *__restrict__ a0,
-                               float *__restrict__ Z) {
+                               const long long *__restrict__ zld, const long long *__restrict__ T,
+                               const long long *__restrict__ a0, float *__restrict__ Z) {
   __shared__ float tile[32][33];
   const int r = blockIdx.z;
   const long long Tr = T[r];
@@ -75,9 +87,10 @@ __global__ void stage_z_kernel(const float *__restrict__ z, const long long *__r
   if (t0 >= Tr) return;
   const int c0 = blockIdx.y * 32;
   const float *zr = z + zoff[r];
+  const long long ld = zld[r];
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const long long t = t0 + threadIdx.x;
-    tile[i][threadIdx.x] = t < Tr ? zr[(long long)(c0 + i) * Tr + t] : 0.0f;
+    tile[i][threadIdx.x] = t < Tr ? zr[(long long)(c0 + i) * ld + t] : 0.0f;
   }
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -87,6 +100,7 @@ __global__ void stage_z_kernel(const float *__restrict__ z, const long long *__r
 }
 
 struct Plan {
+  std::vector<pt_b200_window> W;   // the requests this plan lays out
   std::vector<int64_t> T;
   int64_t R[3] = {0, 0, 0};
   int64_t max_T = 0, total_z = 0, total_wav = 0;
@@ -94,8 +108,8 @@ struct Plan {
   unsigned char *mask[3] = {nullptr, nullptr, nullptr};
   unsigned char *mask_refl = nullptr, *mask_post = nullptr;
   int *ob01 = nullptr, *ob12 = nullptr;
-  long long *zoff = nullptr, *Td = nullptr, *a0 = nullptr;
-  long long *row0 = nullptr, *tp = nullptr, *wav0 = nullptr;
+  long long *zoff = nullptr, *zld = nullptr, *Td = nullptr, *a0 = nullptr;
+  long long *row0 = nullptr, *tp = nullptr, *wav0 = nullptr, *klo = nullptr, *khi = nullptr;
   void *table_block = nullptr;
   size_t table_bytes = 0;
 };
@@ -111,6 +125,7 @@ struct pt_b200_decoder {
   std::mutex mu;
   Plan plan;
   bool have_plan = false;
+  cudaEvent_t done = nullptr;   // recorded after every decode: plan changes wait for it
   // activation buffers (grown on demand, zeroed when the plan changes)
   void *act = nullptr;
   size_t act_bytes = 0;
@@ -129,26 +144,54 @@ struct pt_b200_decoder {
 
 namespace {
 
-int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
+bool same_windows(const std::vector<pt_b200_window> &a, int n, const pt_b200_window *w) {
+  if ((int)a.size() != n) return false;
+  for (int i = 0; i < n; ++i)
+    if (a[i].frames != w[i].frames || a[i].z_off != w[i].z_off || a[i].z_ld != w[i].z_ld ||
+        a[i].keep_lo != w[i].keep_lo || a[i].keep_hi != w[i].keep_hi || a[i].dst != w[i].dst)
+      return false;
+  return true;
+}
+
+int check_windows(int n, const pt_b200_window *w) {
+  PTB_REQUIRE(n > 0 && w, "pt_b200: no requests");
+  for (int i = 0; i < n; ++i) {
+    const pt_b200_window &x = w[i];
+    PTB_REQUIRE(x.frames >= 2, "pt_b200: request %d has %lld frames (need >= 2)", i,
+                (long long)x.frames);
+    PTB_REQUIRE(x.z_off >= 0 && x.z_ld >= x.frames, "pt_b200: request %d: bad latent slice", i);
+    PTB_REQUIRE(x.keep_lo >= 0 && x.keep_lo < x.keep_hi && x.keep_hi <= 256 * x.frames && x.dst >= 0,
+                "pt_b200: request %d: kept samples [%lld, %lld) outside [0, %lld)", i,
+                (long long)x.keep_lo, (long long)x.keep_hi, (long long)(256 * x.frames));
+  }
+  return 0;
+}
+
+// Lay the requests out (masks, convT row maps, per-request tables) unless the previous plan had
+// the same requests.  A new plan first waits for the last decode that used the old one (any
+// stream), then uploads and zeroes on `st`, so later work on `st` is ordered after it.
+int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_window *w) {
   Plan &p = d->plan;
-  if (d->have_plan && (int)p.T.size() == nreq && std::memcmp(p.T.data(), T, sizeof(int64_t) * nreq) == 0)
-    return 0;
+  if (d->have_plan && same_windows(p.W, nreq, w)) return 0;
+  if (check_windows(nreq, w)) return -1;
+  if (d->done) PTB_CUDA(cudaEventSynchronize(d->done));
   if (p.table_block) cudaFree(p.table_block);
   d->have_plan = false;
   p = Plan();
-  p.T.assign(T, T + nreq);
+  p.W.assign(w, w + nreq);
+  for (int i = 0; i < nreq; ++i) p.T.push_back(w[i].frames);
+  const int64_t *T = p.T.data();
   const int64_t scale[3] = {1, 4, 16};
   std::vector<int64_t> a[3];
   for (int l = 0; l < 3; ++l) {
-    int64_t off = kGap;
+    int64_t off = kGap[l];
     for (int i = 0; i < nreq; ++i) {
       a[l].push_back(off);
-      off += scale[l] * T[i] + kGap;
+      off += scale[l] * T[i] + kGap[l];
     }
     p.R[l] = off;
   }
   for (int i = 0; i < nreq; ++i) {
-    PTB_REQUIRE(T[i] >= 2, "pt_b200: request %d has %lld frames (need >= 2)", i, (long long)T[i]);
     p.max_T = T[i] > p.max_T ? T[i] : p.max_T;
     p.total_z += 192 * T[i];
     p.total_wav += 256 * T[i];
@@ -158,7 +201,7 @@ int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
                   p.R[1] * 256 < (int64_t)INT_MAX,
               "pt_b200: batch too large (%lld level-2 rows); split it into smaller batches",
               (long long)p.R[2]);
-  // host tables in one pinned block
+  // host tables in one block
   std::vector<unsigned char> m[3], mr, mp;
   for (int l = 0; l < 3; ++l) m[l].assign((size_t)p.R[l], 0);
   for (int l = 0; l < 3; ++l)
@@ -180,25 +223,28 @@ int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
       ob12[(size_t)(a[1][i] + q)] = (int)(a[2][i] - 4 * a[1][i] - 6);
     }
   }
-  std::vector<long long> zoff(nreq), Td(nreq), a0(nreq), row0(nreq), tp(nreq), wav0(nreq);
-  long long zo = 0, wo = 0;
+  // per-request tables: z offset, z channel stride, frames, level-0 row, conv_post first row,
+  // tail frames, wav offset (dst - keep_lo), kept sample range
+  constexpr int kTab = 9;
+  std::vector<long long> tab((size_t)kTab * nreq);
   for (int i = 0; i < nreq; ++i) {
-    zoff[i] = zo;
-    Td[i] = T[i];
-    a0[i] = a[0][i];
-    row0[i] = a[2][i] - 1;
-    tp[i] = 16 * T[i] + 1;
-    wav0[i] = wo;
-    zo += 192 * T[i];
-    wo += 256 * T[i];
+    long long *t = tab.data();
+    t[0 * nreq + i] = w[i].z_off;
+    t[1 * nreq + i] = w[i].z_ld;
+    t[2 * nreq + i] = T[i];
+    t[3 * nreq + i] = a[0][i];
+    t[4 * nreq + i] = a[2][i] - 1;
+    t[5 * nreq + i] = 16 * T[i] + 1;
+    t[6 * nreq + i] = w[i].dst - w[i].keep_lo;
+    t[7 * nreq + i] = w[i].keep_lo;
+    t[8 * nreq + i] = w[i].keep_hi;
   }
   // one device block: masks, convT row maps, per-request tables
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-  size_t off[12], tot = 0;
-  const size_t sz[12] = {(size_t)p.R[0], (size_t)p.R[1], (size_t)p.R[2], (size_t)p.R[2],
-                         (size_t)p.R[2], ob01.size() * 4, ob12.size() * 4, (size_t)nreq * 8,
-                         (size_t)nreq * 8, (size_t)nreq * 8, (size_t)nreq * 8, (size_t)nreq * 24};
-  for (int k = 0; k < 12; ++k) {
+  size_t off[8], tot = 0;
+  const size_t sz[8] = {(size_t)p.R[0], (size_t)p.R[1], (size_t)p.R[2], (size_t)p.R[2],
+                        (size_t)p.R[2], ob01.size() * 4, ob12.size() * 4, tab.size() * 8};
+  for (int k = 0; k < 8; ++k) {
     off[k] = tot;
     tot += al(sz[k]);
   }
@@ -212,25 +258,23 @@ int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
   std::memcpy(host.data() + off[4], mp.data(), sz[4]);
   std::memcpy(host.data() + off[5], ob01.data(), sz[5]);
   std::memcpy(host.data() + off[6], ob12.data(), sz[6]);
-  std::memcpy(host.data() + off[7], zoff.data(), sz[7]);
-  std::memcpy(host.data() + off[8], Td.data(), sz[8]);
-  std::memcpy(host.data() + off[9], a0.data(), sz[9]);
-  std::memcpy(host.data() + off[10], row0.data(), sz[10]);
-  std::memcpy(host.data() + off[11], tp.data(), (size_t)nreq * 8);
-  std::memcpy(host.data() + off[11] + (size_t)nreq * 8, wav0.data(), (size_t)nreq * 8);
-  PTB_CUDA(cudaMemcpyAsync(base, host.data(), tot, cudaMemcpyHostToDevice, d->stream));
-  PTB_CUDA(cudaStreamSynchronize(d->stream));
+  std::memcpy(host.data() + off[7], tab.data(), sz[7]);
+  PTB_CUDA(cudaMemcpyAsync(base, host.data(), tot, cudaMemcpyHostToDevice, st));
   for (int l = 0; l < 3; ++l) p.mask[l] = reinterpret_cast<unsigned char *>(base + off[l]);
   p.mask_refl = reinterpret_cast<unsigned char *>(base + off[3]);
   p.mask_post = reinterpret_cast<unsigned char *>(base + off[4]);
   p.ob01 = reinterpret_cast<int *>(base + off[5]);
   p.ob12 = reinterpret_cast<int *>(base + off[6]);
-  p.zoff = reinterpret_cast<long long *>(base + off[7]);
-  p.Td = reinterpret_cast<long long *>(base + off[8]);
-  p.a0 = reinterpret_cast<long long *>(base + off[9]);
-  p.row0 = reinterpret_cast<long long *>(base + off[10]);
-  p.tp = reinterpret_cast<long long *>(base + off[11]);
-  p.wav0 = reinterpret_cast<long long *>(base + off[11] + (size_t)nreq * 8);
+  long long *tb = reinterpret_cast<long long *>(base + off[7]);
+  p.zoff = tb;
+  p.zld = tb + nreq;
+  p.Td = tb + 2 * nreq;
+  p.a0 = tb + 3 * nreq;
+  p.row0 = tb + 4 * nreq;
+  p.tp = tb + 5 * nreq;
+  p.wav0 = tb + 6 * nreq;
+  p.klo = tb + 7 * nreq;
+  p.khi = tb + 8 * nreq;
   p.table_bytes = tot;
 
   // activation buffers: grow if needed, then zero (gap rows must read as zeros)
@@ -259,7 +303,8 @@ int build_plan(pt_b200_decoder *d, int nreq, const int64_t *T) {
   d->P = take(r2 * 128);
   d->POST = take(r2 * 80);
   PTB_CUDA(cudaMemsetAsync(d->act, 0, (size_t)(reinterpret_cast<char *>(q) - static_cast<char *>(d->act)),
-                           d->stream));
+                           st));
+  // (a copy from pageable memory returns once the source is staged: `host` may go)
   d->have_plan = true;
   return 0;
 }
@@ -321,7 +366,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
     dim3 grid((unsigned)((p.max_T + 31) / 32), 192 / 32, (unsigned)nreq);
-    stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.Td, p.a0, d->Z);
+    stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.zld, p.Td, p.a0, d->Z);
     PTB_CUDA(cudaGetLastError());
     count_launch();
   }
@@ -401,9 +446,11 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   }
   // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
   rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);
-  if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, nreq, 16 * p.max_T + 1, d->pqmf, wav_dev, st))
+  if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, p.klo, p.khi, nreq, 16 * p.max_T + 1,
+                    d->pqmf, wav_dev, st))
     return -1;
   if (d->prof) cudaEventRecord(d->ev[d->nrec], st);
+  PTB_CUDA(cudaEventRecord(d->done, st));
   return 0;
 }
 
@@ -432,7 +479,9 @@ pt_b200_decoder *pt_b200_decoder_create(int device, const pt_b200_dec_weights *w
     pt_b200_decoder_destroy(d);
     return static_cast<pt_b200_decoder *>(nullptr);
   };
-  if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+  if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&d->done, cudaEventDisableTiming) != cudaSuccess)
+    return fail("stream");
   if (cudaMalloc(&d->gerr, 4) != cudaSuccess || cudaMemset(d->gerr, 0, 4) != cudaSuccess ||
       cudaMallocHost(&d->gerr_host, 4) != cudaSuccess)
     return fail("error word");
@@ -483,22 +532,101 @@ void pt_b200_decoder_destroy(pt_b200_decoder *d) {
   if (d->gerr_host) cudaFreeHost(d->gerr_host);
   for (auto &e : d->ev)
     if (e) cudaEventDestroy(e);
+  if (d->done) cudaEventDestroy(d->done);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
+}
+
+int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n, const pt_b200_window *w,
+                           const float *z_dev, float *wav_dev) {
+  PTB_REQUIRE(d && w && z_dev && wav_dev && n > 0, "pt_b200: bad decode arguments");
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
+  if (build_plan(d, st, n, w)) return -1;
+  return run_decoder(d, st, z_dev, wav_dev);
 }
 
 int pt_b200_decode_batch_device(pt_b200_decoder *d, void *stream, int nreq, const int64_t *T,
                                 const float *z_dev, float *wav_dev) {
   PTB_REQUIRE(d && T && z_dev && wav_dev && nreq > 0, "pt_b200: bad decode arguments");
-  std::lock_guard<std::mutex> lk(d->mu);
-  PTB_CUDA(cudaSetDevice(d->device));
-  cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
-  if (build_plan(d, nreq, T)) return -1;
-  if (st != d->stream) {
-    // plan uploads ran on the decoder stream: order them before work on the caller's stream
-    PTB_CUDA(cudaStreamSynchronize(d->stream));
+  // whole utterances: request i reads its own [192][T_i] block and keeps every sample
+  std::vector<pt_b200_window> w((size_t)nreq);
+  int64_t zo = 0, wo = 0;
+  for (int i = 0; i < nreq; ++i) {
+    w[i].frames = T[i];
+    w[i].z_off = zo;
+    w[i].z_ld = T[i];
+    w[i].keep_lo = 0;
+    w[i].keep_hi = 256 * T[i];
+    w[i].dst = wo;
+    zo += 192 * T[i];
+    wo += 256 * T[i];
   }
-  return run_decoder(d, st, z_dev, wav_dev);
+  return pt_b200_decode_windows(d, stream, nreq, w.data(), z_dev, wav_dev);
+}
+
+int64_t pt_b200_stream_plan(int nstreams, const int64_t *T, int win, int ctx, int exact,
+                            pt_b200_window *out, int64_t cap) {
+  PTB_REQUIRE(nstreams > 0 && T && win > 0 && ctx >= 0 && (cap == 0 || out),
+              "pt_b200: bad stream plan arguments");
+  const int64_t step = win - 2 * ctx > 1 ? win - 2 * ctx : 1;
+  int64_t nw = 0, zo = 0, wo = 0;
+  auto put = [&](int64_t a, int64_t frames, int64_t lo, int64_t hi, int64_t dst, int64_t Ts) {
+    if (nw < cap) out[nw] = pt_b200_window{frames, zo + a, Ts, lo, hi, dst};
+    ++nw;
+  };
+  for (int s = 0; s < nstreams; ++s) {
+    const int64_t Ts = T[s];
+    PTB_REQUIRE(Ts >= 2, "pt_b200: stream %d has %lld frames (need >= 2)", s, (long long)Ts);
+    if (!exact) {
+      // the reference's overlap-save loop (runtime/v21/src/main_v21.c:342-364)
+      int64_t olen = 0;
+      for (int64_t a = 0;; a += step) {
+        const int64_t we = a + win > Ts ? Ts - a : win;
+        const bool first = a == 0, last = a + we >= Ts;
+        const int64_t n = 256 * we;
+        const int64_t lo = first ? 0 : 256 * (int64_t)ctx;
+        int64_t hi = last ? n : 256 * (we - ctx);
+        if (hi > n) hi = n;
+        if (hi > lo) {
+          put(a, we, lo, hi, wo + olen, Ts);
+          olen += hi - lo;
+        }
+        if (last) break;
+      }
+    } else {
+      // same emission schedule, context widened to the receptive radius
+      const int64_t cl = ctx > kReachLeft ? ctx : kReachLeft, cr = ctx > kReachRight ? ctx : kReachRight;
+      for (int64_t e = 0; e < Ts; e += step) {
+        const int64_t e1 = e + step < Ts ? e + step : Ts;
+        const int64_t a = e - cl > 0 ? e - cl : 0, b = e1 + cr < Ts ? e1 + cr : Ts;
+        put(a, b - a, 256 * (e - a), 256 * (e1 - a), wo + 256 * e, Ts);
+      }
+    }
+    zo += 192 * Ts;
+    wo += 256 * Ts;
+  }
+  return nw;
+}
+
+int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstreams, const int64_t *T,
+                          const float *z_dev, int win, int ctx, int exact, int64_t max_frames,
+                          float *wav_dev) {
+  PTB_REQUIRE(d && T && z_dev && wav_dev && nstreams > 0, "pt_b200: bad stream arguments");
+  const int64_t nw = pt_b200_stream_plan(nstreams, T, win, ctx, exact, nullptr, 0);
+  if (nw < 0) return -1;
+  std::vector<pt_b200_window> w((size_t)nw);
+  pt_b200_stream_plan(nstreams, T, win, ctx, exact, w.data(), nw);
+  if (max_frames <= 0) max_frames = kStreamBatchFrames;
+  // windows in plan order, batched up to max_frames latent frames
+  for (int64_t i = 0; i < nw;) {
+    int64_t j = i, fr = 0;
+    while (j < nw && (j == i || fr + w[j].frames <= max_frames) && j - i < INT_MAX) fr += w[j++].frames;
+    if (pt_b200_decode_windows(d, stream, (int)(j - i), w.data() + i, z_dev, wav_dev)) return -1;
+    i = j;
+  }
+  return 0;
 }
 
 int pt_b200_decoder_sync(pt_b200_decoder *d, void *stream) {

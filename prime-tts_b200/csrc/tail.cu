@@ -43,7 +43,8 @@ struct TailArgs {
   long long st_t, st_c;   //   post[(row0[r] + f) * st_t + c * st_c]
   const long long *row0;  // per request (nullptr: 0)
   const long long *tp;    // per request frame count (nullptr: tp1)
-  const long long *wav0;  // per request output offset (nullptr: 0)
+  const long long *wav0;  // per request output offset (nullptr: 0): sample j goes to wav[wav0 + j]
+  const long long *klo, *khi;   // per request kept samples [klo, khi) (nullptr: all)
   long long tp1;
   const float *pqmf;      // [4][63]
   float *wav;
@@ -64,7 +65,8 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   const long long Tp = a.tp ? a.tp[req] : a.tp1;
   const long long nwav = 16 * (Tp - 1);
   const long long j0 = (long long)blockIdx.x * kTailW;
-  if (Tp < 2 || j0 >= nwav) return;
+  const long long keep_lo = a.klo ? a.klo[req] : 0, keep_hi = a.khi ? a.khi[req] : nwav;
+  if (Tp < 2 || j0 >= nwav || j0 >= keep_hi || j0 + kTailW <= keep_lo) return;
   const long long Ls = 4 * (Tp - 1);
   const float *post = a.post + (a.row0 ? a.row0[req] : 0) * a.st_t;
   // the reference switches Exp/Sin/Cos to fp32 libm only for tensors of >= 4096 elements
@@ -151,8 +153,10 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   float *wav = a.wav + (a.wav0 ? a.wav0[req] : 0);
   const int jn = (int)(nwav - j0 < kTailW ? nwav - j0 : kTailW);
   const int mlo = (int)m_lo, nw = (int)nwav, jb = (int)j0;
+  const int klo = (int)keep_lo, khi = (int)(keep_hi < nwav ? keep_hi : nwav);
   for (int jj = threadIdx.x; jj < jn; jj += blockDim.x) {
     const int j = jb + jj;
+    if (j < klo || j >= khi) continue;
     float acc = 0.0f;
     const int k0 = (31 - j) & 3;  // first tap with (j + k - 31) % 4 == 0
 #pragma unroll 4
@@ -250,10 +254,11 @@ int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wa
   return 0;
 }
 
-// batched requests, channels-last post rows (ld = row stride); per-request tables on the device
+// batched requests, channels-last post rows (ld = row stride); per-request tables on the device,
+// each request writing only its kept samples
 int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
-                  const long long *wav0, int nreq, long long max_tp, const float *pqmf_dev,
-                  float *wav_dev, cudaStream_t st) {
+                  const long long *wav0, const long long *klo, const long long *khi, int nreq,
+                  long long max_tp, const float *pqmf_dev, float *wav_dev, cudaStream_t st) {
   if (tail_ready()) return -1;
   TailArgs a{};
   a.post = post_dev;
@@ -262,6 +267,8 @@ int tail_run_rows(const float *post_dev, long long ld, const long long *row0, co
   a.row0 = row0;
   a.tp = tp;
   a.wav0 = wav0;
+  a.klo = klo;
+  a.khi = khi;
   a.pqmf = pqmf_dev;
   a.wav = wav_dev;
   const long long nwav = 16 * (max_tp - 1);

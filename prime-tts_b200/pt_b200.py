@@ -84,6 +84,12 @@ class DecWeightsC(C.Structure):
 
 
 # exported C symbols and their ctypes signatures
+class WindowC(C.Structure):
+    """pt_b200_window: one streaming window (a latent column slice and the samples it keeps)."""
+    _fields_ = [("frames", C.c_int64), ("z_off", C.c_int64), ("z_ld", C.c_int64),
+                ("keep_lo", C.c_int64), ("keep_hi", C.c_int64), ("dst", C.c_int64)]
+
+
 _SIGS = {
     "pt_v21_cuda_prewarm": ([], C.c_int),
     "pt_v21_cuda_init": ([C.c_void_p, C.c_int], C.c_int),
@@ -120,6 +126,12 @@ _SIGS = {
     "pt_b200_decode_batch_device": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p,
                                      C.c_void_p], C.c_int),
     "pt_b200_decoder_sync": ([C.c_void_p, C.c_void_p], C.c_int),
+    "pt_b200_decode_windows": ([C.c_void_p, C.c_void_p, C.c_int, C.POINTER(WindowC), C.c_void_p,
+                                C.c_void_p], C.c_int),
+    "pt_b200_stream_plan": ([C.c_int, _i64p, C.c_int, C.c_int, C.c_int, C.POINTER(WindowC),
+                             _i64], _i64),
+    "pt_b200_stream_decode": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p, C.c_int,
+                               C.c_int, C.c_int, _i64, C.c_void_p], C.c_int),
     "pt_b200_decoder_profile": ([C.c_void_p, C.c_int], C.c_int),
     "pt_b200_decoder_launch_times": ([C.c_void_p, C.c_int, C.POINTER(C.c_double),
                                       C.POINTER(C.c_double), C.POINTER(C.c_double),
@@ -385,6 +397,28 @@ def config4(seed: int = 3, n: int = 64, lo: int = 50, hi: int = 600):
     return [int(t) for t in T], zs
 
 
+def config5(seed: int = 4, n: int = 512, lo: int = 100, hi: int = 1000):
+    """Config 5: n streams, T ~ U{lo..hi} (inclusive integers), z ~ N(0,1) per stream; decoded in
+    64-frame windows with 16 frames of context per side (step 32)."""
+    return config4(seed, n, lo, hi)
+
+
+STREAM_WIN, STREAM_CTX = 64, 16
+
+
+def stream_plan(T, win: int = STREAM_WIN, ctx: int = STREAM_CTX, exact: bool = False) -> np.ndarray:
+    """The library's window plan (pt_b200_stream_plan) as an int64 array of rows
+    (frames, z_off, z_ld, keep_lo, keep_hi, dst) over concatenated latents / waveforms."""
+    T = np.ascontiguousarray(T, np.int64)
+    n = lib().pt_b200_stream_plan(len(T), T.ctypes.data_as(_i64p), win, ctx, int(exact), None, 0)
+    if n < 0:
+        _check(-1, "pt_b200_stream_plan")
+    arr = (WindowC * max(n, 1))()
+    lib().pt_b200_stream_plan(len(T), T.ctypes.data_as(_i64p), win, ctx, int(exact), arr, n)
+    return np.array([[w.frames, w.z_off, w.z_ld, w.keep_lo, w.keep_hi, w.dst] for w in arr[:n]],
+                    np.int64).reshape(-1, 6)
+
+
 def decoder_gflop(T: int) -> float:
     """Algorithmic GFLOP of one decoder request of T frames (2 x MACs; convT counted without the
     zero-stuffed MACs; the tail's einsum / OLA / PQMF included)."""
@@ -462,6 +496,43 @@ class Decoder:
         _check(lib().pt_b200_decode_batch_device(self.h, stream, len(T),
                                                  T.ctypes.data_as(_i64p), z_dev, wav_dev),
                "pt_b200_decode_batch_device")
+
+    def decode_windows(self, windows: np.ndarray, z_dev: int, wav_dev: int, stream=None) -> None:
+        """Windows given as rows (frames, z_off, z_ld, keep_lo, keep_hi, dst); device buffers."""
+        w = np.ascontiguousarray(windows, np.int64).reshape(-1, 6)
+        arr = (WindowC * len(w))(*[WindowC(*map(int, r)) for r in w])
+        _check(lib().pt_b200_decode_windows(self.h, stream, len(w), arr, z_dev, wav_dev),
+               "pt_b200_decode_windows")
+
+    def stream_device(self, T, z_dev: int, wav_dev: int, win: int = STREAM_WIN,
+                      ctx: int = STREAM_CTX, exact: bool = False, max_frames: int = 0,
+                      stream=None) -> None:
+        """Decode and stitch every stream (concatenated [192][T_i] latents -> concatenated
+        [256*T_i] waveforms, device buffers), asynchronous on `stream`."""
+        T = np.ascontiguousarray(T, np.int64)
+        _check(lib().pt_b200_stream_decode(self.h, stream, len(T), T.ctypes.data_as(_i64p), z_dev,
+                                           win, ctx, int(exact), int(max_frames), wav_dev),
+               "pt_b200_stream_decode")
+
+    def stream(self, zs: list, win: int = STREAM_WIN, ctx: int = STREAM_CTX,
+               exact: bool = False, max_frames: int = 0) -> list:
+        """Host in, host out: each stream's z [192][T_i] -> stitched wav [256*T_i]."""
+        import torch
+        T = np.array([z.shape[-1] for z in zs], np.int64)
+        zcat = np.concatenate([np.ascontiguousarray(z, np.float32).ravel() for z in zs])
+        dev = torch.device("cuda", self.device)
+        z_dev = torch.from_numpy(zcat).to(dev)
+        wav_dev = torch.full((int(256 * T.sum()),), float("nan"), device=dev)
+        s = torch.cuda.Stream(device=dev)
+        self.stream_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), win, ctx, exact, max_frames,
+                           s.cuda_stream)
+        self.sync(s.cuda_stream)
+        wav = wav_dev.cpu().numpy()
+        out, o = [], 0
+        for t in T:
+            out.append(wav[o:o + 256 * int(t)])
+            o += 256 * int(t)
+        return out
 
     def sync(self, stream=None) -> None:
         _check(lib().pt_b200_decoder_sync(self.h, stream), "pt_b200_decoder_sync")

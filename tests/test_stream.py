@@ -1,0 +1,96 @@
+"""Streaming window plans and the exactness argument, on the CPU.
+
+The library's overlap-save plan (pt_b200_stream_plan, exact = 0) must be the reference driver's
+loop (runtime/v21/src/main_v21.c:342-364, restated in oracle.overlap_save_windows).  The exact
+plan keeps that emission schedule and widens every window to the decoder's receptive radius
+(25 frames back, 24 ahead); decoding its windows with the CPU oracle and stitching them must give
+the whole-utterance decode bit for bit, while the reference's (64, 16) scheme does not.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import pt_b200
+
+CASES_T = [2, 20, 33, 48, 63, 64, 65, 96, 97, 100, 129, 1000]
+SCHEMES = [(64, 16), (48, 16), (64, 8), (256, 16), (81, 25)]
+
+
+@pytest.mark.parametrize("win,ctx", SCHEMES)
+def test_overlap_save_plan_is_the_reference_loop(win, ctx):
+    plan = pt_b200.stream_plan(CASES_T, win, ctx, exact=False)
+    k, zo, wo = 0, 0, 0
+    for T in CASES_T:
+        olen = 0
+        for a, we, lo, hi in oracle.overlap_save_windows(T, win, ctx):
+            frames, z_off, z_ld, klo, khi, dst = plan[k]
+            assert (frames, z_off, z_ld, klo, khi, dst) == (we, zo + a, T, lo, hi, wo + olen)
+            olen += hi - lo
+            k += 1
+        assert olen == 256 * T   # the reference loop emits every sample once
+        zo += 192 * T
+        wo += 256 * T
+    assert k == len(plan)
+
+
+@pytest.mark.parametrize("win,ctx", SCHEMES)
+def test_exact_plan_covers_and_has_full_context(win, ctx):
+    plan = pt_b200.stream_plan(CASES_T, win, ctx, exact=True)
+    step = max(1, win - 2 * ctx)
+    cl, cr = max(ctx, 25), max(ctx, 24)
+    k, zo, wo = 0, 0, 0
+    for T in CASES_T:
+        nxt = 0   # next sample of this stream to emit
+        for e in range(0, T, step):
+            frames, z_off, z_ld, klo, khi, dst = plan[k]
+            a = z_off - zo
+            e1 = min(T, e + step)
+            assert z_ld == T and frames >= 2 and 0 <= a and a + frames <= T
+            assert dst == wo + 256 * e == wo + nxt            # contiguous, in order
+            assert (klo, khi) == (256 * (e - a), 256 * (e1 - a))
+            assert e - a >= min(cl, e) and a + frames - e1 >= min(cr, T - e1)
+            nxt = 256 * e1
+            k += 1
+        assert nxt == 256 * T
+        zo += 192 * T
+        wo += 256 * T
+    assert k == len(plan)
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return pt_b200.config3()[0]
+
+
+def test_exact_scheme_is_bit_exact_on_the_oracle(weights):
+    """Stitched exact windows == whole decode, bitwise, on the reference-exact CPU oracle; the
+    same windows with one frame less of right context already differ."""
+    orc = oracle.CpuDecoder("oracle")
+    T = 90
+    z = np.random.default_rng(11).standard_normal((192, T)).astype(np.float32)
+    full = orc.decode(weights, z)
+    plan = pt_b200.stream_plan([T], 64, 16, exact=True)
+    wins = [(int(r[1]), int(r[0]), int(r[3]), int(r[4])) for r in plan]
+    got = oracle.stitch(lambda zz: orc.decode(weights, zz), z, wins)
+    np.testing.assert_array_equal(got, full)
+    # the interior window with its right context cut to 23 frames is no longer exact
+    a, we, lo, hi = wins[1]
+    short = orc.decode(weights, np.ascontiguousarray(z[:, a:a + we - (we - hi // 256 - 23)]))
+    assert not np.array_equal(short[lo:hi], full[256 * 32: 256 * 64])
+
+
+def test_reference_scheme_deviation_on_the_reference_cpu(weights, ref_available):
+    """The reference's own CPU decoder, stitched with its (64, 16) overlap-save loop, deviates
+    from its whole decode by far more than 1e-6 on these weights (the receptive radius is 25
+    frames, the context 16)."""
+    kind = "reference" if ref_available else "oracle"
+    dec = oracle.CpuDecoder(kind)
+    T = 80
+    z = np.random.default_rng(12).standard_normal((192, T)).astype(np.float32)
+    full = dec.decode(weights, z)
+    got = oracle.stitch(lambda zz: dec.decode(weights, zz), z, oracle.overlap_save_windows(T, 64, 16))
+    m = oracle.metrics(got, full)
+    print(f"reference CPU ({kind}) overlap-save (64,16) vs whole decode, T={T}: "
+          f"max|d| {m['max_abs']:.3e}  SNDR {m['sndr_db']:.1f} dB")
+    assert got.shape == full.shape
+    assert m["max_abs"] > 1e-6 and m["sndr_db"] > 20.0
