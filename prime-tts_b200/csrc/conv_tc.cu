@@ -81,6 +81,24 @@ int make_map_w(CUtensorMap *m, const float *base, int64_t krow, int64_t nrows, i
   return 0;
 }
 
+// Output map of a rows-mode epilogue: [rows][ld] fp32, tiles of 16 rows x 32 channels, no swizzle
+// (the staging tile is row-major, 128 bytes a row).
+int make_map_out(CUtensorMap *m, const float *base, int ld, int64_t rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (encoder(&enc)) return -1;
+  PTB_REQUIRE(base && (reinterpret_cast<uintptr_t>(base) & 15) == 0 && ld % 4 == 0 && rows > 0,
+              "pt_b200: output map needs a 16-byte aligned base and rows of 4k floats");
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, 16};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PTB_REQUIRE(r == CUDA_SUCCESS, "pt_b200: output tensor map encode failed (%d)", (int)r);
+  return 0;
+}
+
 // ---------------------------------------------------------------------------- instances
 // N tiles compiled: the decoder needs 256 (256/512-channel layers, upsamplers), 128 (128-channel
 // layers) and 80 (conv_post, 72 channels); 16/32/64 serve the small tail convs and generic calls.
@@ -193,29 +211,40 @@ static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
 
 template <int MODE, int F>
 static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(conv_tc_tn_kernel<MODE, F>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg::kBytes);
-  });
-  PTB_CUDA(attr_err);
+  // the shared-memory opt-in is per device
+  static std::mutex mu;
+  static unsigned long long attr_done = 0;
+  int dev = 0;
+  PTB_CUDA(cudaGetDevice(&dev));
+  PTB_REQUIRE(dev >= 0 && dev < 64, "pt_b200: device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!((attr_done >> dev) & 1ull)) {
+      PTB_CUDA(cudaFuncSetAttribute(conv_tc_tn_kernel<MODE, F>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg::kBytes));
+      attr_done |= 1ull << dev;
+    }
+  }
   static int sms = 0;
   if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, to0, to1;
+  std::memset(&to0, 0, sizeof(to0));
+  std::memset(&to1, 0, sizeof(to1));
   if (make_map_act(&tx, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
   if (make_map_w(&tw, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, kBM)) return -1;
+  if constexpr (TNTmaStore<MODE, F>::value) {
+    if ((F & EF_OUT0) && make_map_out(&to0, L.e.out0, L.e.ldc, L.g.m_rows)) return -1;
+    if ((F & EF_OUT1) && make_map_out(&to1, L.e.out1, L.e.ldc1, L.g.m_rows)) return -1;
+  }
   const long long tiles = (long long)((L.g.n_cols + kBM - 1) / kBM) *
                           ((L.g.m_rows + kTNRows - 1) / kTNRows) * L.batch;
   ConvGeom g = L.g;
   g.nbatch = L.batch;
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg::kBytes, st>>>(tx, tw, g, L.e, gerr);
+  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;

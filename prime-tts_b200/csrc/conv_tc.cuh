@@ -889,8 +889,18 @@ struct TNCfg {
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
-  static constexpr int kAStages = 8;
-  static constexpr int kBytes = 2 * kWinBytes + kAStages * kA + 1024 + 256;
+  static constexpr int kAStages = 7;
+  static constexpr int kStageWarp = 2 * 16 * kBK * 4;             // 2 x (16 rows x 32 channels)
+  static constexpr int kStage = 8 * kStageWarp;                   // 32 KiB output staging
+  static constexpr int kBytes = 2 * kWinBytes + kAStages * kA + kStage + 1024 + 256;
+};
+
+// Instances whose outputs leave through TMA tile stores staged in shared memory: the rows-mode
+// decoder epilogues except the one that also writes the reflection row (that row lies in a gap
+// that the staged stores of its neighbours would zero).
+template <int MODE, int F>
+struct TNTmaStore {
+  static constexpr bool value = MODE == EPI_ROWS && F != EF_GENERIC && (F & EF_REFL) == 0;
 };
 
 // Plain-mode (interpreter ABI) epilogue of one 32-channel x 32-row block: this thread's channel
@@ -984,17 +994,56 @@ __device__ __forceinline__ void tn_rows_load(const EpiParams &e, int th, int col
 // One 16-row pass: rows th .. th+15 are TMEM columns taddr .. taddr+15.  `mk` is this lane's row
 // mask in the pass's 32-row block (bit 0 store, bit 1 also store the reflected row) and
 // `orow_blk` its output row (row-map mode).
+// With TMA stores (TNTmaStore) the pass writes its 16 rows x 32 channels into this warp's
+// staging slots (row-major 16 x 128 B, conflict-free) and one lane issues the tile stores; masked
+// rows are written as zeros, which keeps gap rows zero.  One output tensor alternates between the
+// two slots (its previous store may still be reading the other); two tensors take one slot each.
 template <int MODE, int F>
 __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr, int th, int h,
                                              int col, bool colok, float bias, unsigned mk,
                                              int orow_blk, const float (&rs)[16],
-                                             const float (&ac)[16]) {
+                                             const float (&ac)[16], const CUtensorMap *tm0,
+                                             const CUtensorMap *tm1, uint32_t stage, int &slot,
+                                             int lane) {
   using FL = TNRowsFlags<MODE, F>;
   const bool hr = FL::res(e), o0 = FL::out0(e), o1 = FL::out1(e), hrefl = FL::refl(e);
   const int am = FL::acc(e);
   const unsigned valid = __ballot_sync(0xffffffffu, mk & 1u);
   const unsigned vh = (valid >> (16 * h)) & 0xffffu;
   if (!vh) return;   // uniform over the warp: nothing of this pass is stored
+  if constexpr (TNTmaStore<MODE, F>::value) {
+    constexpr bool two = (F & EF_OUT0) && (F & EF_OUT1);
+    const int col0 = col - lane;
+    float v[16];
+    tmem_ld16(taddr, v);
+    if (lane == 0) {
+      if (two) bulk_wait_read<0>();
+      else bulk_wait_read<1>();
+    }
+    __syncwarp();
+    const uint32_t s0 = stage + (two ? 0u : static_cast<uint32_t>(slot) * (16 * kBK * 4));
+    const uint32_t s1 = two ? stage + 16 * kBK * 4 : s0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const bool ok = ((vh >> i) & 1) && colok;
+      float x = v[i] + bias;
+      if (hr) x += rs[i];
+      if (am == 2) x = ac[i] + x;
+      else if (am == 3) x = (ac[i] + x) / 3.0f;
+      const uint32_t at = static_cast<uint32_t>(i * kBK * 4 + lane * 4);
+      if (o0) st_shared_f32(s0 + at, ok ? x : 0.0f);
+      if (o1) st_shared_f32(s1 + at, ok ? tf32_rna(leaky(x, e.alpha1)) : 0.0f);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && col0 < e.nstore) {
+      if (o0) tma_store_2d(tm0, s0, col0, th);
+      if (o1) tma_store_2d(tm1, s1, col0, th);
+      bulk_commit();
+    }
+    slot ^= 1;
+    return;
+  }
   const unsigned rh =
       hrefl ? (__ballot_sync(0xffffffffu, (mk >> 1) & 1u) >> (16 * h)) & 0xffffu : 0u;
   const int ldc = e.ldc, ldc1 = e.ldc1;
@@ -1024,7 +1073,9 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
 template <int MODE, int F>
 __global__ void __launch_bounds__(kTNThreads, 1)
     conv_tc_tn_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                      const ConvGeom g, const EpiParams e, uint32_t *gerr) {
+                      const __grid_constant__ CUtensorMap tmO0,
+                      const __grid_constant__ CUtensorMap tmO1, const ConvGeom g, const EpiParams e,
+                      uint32_t *gerr) {
   using P = TNCfg;
   constexpr int AS = P::kAStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1032,7 +1083,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
   const uint32_t win0 = base, ast0 = base + 2 * P::kWinBytes;
-  const uint32_t bar0 = ast0 + AS * P::kA;
+  const uint32_t stg0 = ast0 + AS * P::kA;   // epilogue output staging, kStageWarp per warp
+  const uint32_t bar0 = stg0 + P::kStage;
   auto wfull = [&](int s) { return bar0 + 8u * s; };
   auto wempty = [&](int s) { return bar0 + 8u * (2 + s); };
   auto afull = [&](int s) { return bar0 + 8u * (4 + s); };   // accumulator ready
@@ -1183,6 +1235,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   } else {
     // ---------------- epilogue warps 0..7: lane quarter (channels) x time half
     const int q = warp & 3, half = warp >> 2;
+    const uint32_t stg = stg0 + static_cast<uint32_t>(warp) * P::kStageWarp;
+    int slot = 0;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int ab = it & 1;
@@ -1229,10 +1283,11 @@ __global__ void __launch_bounds__(kTNThreads, 1)
           const int oj = j == 0 ? orow[0] : j == 1 ? orow[1] : j == 2 ? orow[2] : orow[3];
           float rsB[16], acB[16];
           tn_rows_load<MODE, F>(e, th + 16, col, colok, g.m_rows, rsB, acB);
-          tn_rows_pass<MODE, F>(e, tw + 32u * j, th, 0, col, colok, bias, mj, oj, rsA, acA);
+          tn_rows_pass<MODE, F>(e, tw + 32u * j, th, 0, col, colok, bias, mj, oj, rsA, acA, &tmO0,
+                                &tmO1, stg, slot, lane);
           if (j < 3) tn_rows_load<MODE, F>(e, th + 32, col, colok, g.m_rows, rsA, acA);
           tn_rows_pass<MODE, F>(e, tw + 32u * j + 16u, th + 16, 1, col, colok, bias, mj, oj, rsB,
-                                acB);
+                                acB, &tmO0, &tmO1, stg, slot, lane);
         }
       } else {
         if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
@@ -1244,6 +1299,10 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(aempty(ab));
+    }
+    if constexpr (TNTmaStore<MODE, F>::value) {
+      if (lane == 0) bulk_wait_all();   // staged stores done before the CTA's memory goes
+      __syncwarp();
     }
   }
   tc_fence_before();
