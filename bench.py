@@ -9,12 +9,21 @@ no collective on the data path ("scaling": "weak").  One step = one batched deco
 requests (every layer of every request, the iSTFT/PQMF tail included).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload batch|stream] [--layers] [--traffic-from CSV]
 
 `value` is device-resident throughput (z and the waveform in HBM, CUDA events around K steps,
 L2 flushed between steps, max over ranks).  `e2e` is the same metric through the C ABI's host
 entry point (pt_b200_decode_batch): pinned host latents in, host waveform out, copies inside the
 timed region.  `--impl reference` times the reference's own CPU decoder (oracle/_ref, compiled
 from its sources) on all host cores, on a bounded sample of the same workload.
+
+`--workload stream` measures BASELINE config 5 instead: 512 streams per GPU, T ~ U{100..1000}
+(default_rng(4)), decoded in 64-frame windows with 16 frames of context per side and stitched
+(pt_b200_stream_decode, exact scheme: context widened to the 25/24-frame receptive radius, so the
+output equals a whole-utterance decode); only emitted (useful) audio counts.  `--layers` prints
+the per-layer table (time, TFLOP/s, GB/s and both roofline bounds) of one decode instead of the
+bench line.  `--traffic-from CSV` turns an ncu capture of the conv kernel's DRAM bytes into
+profiles/conv_tc_traffic.json (the roofline's `traffic`).
 """
 import argparse
 import datetime
@@ -50,6 +59,12 @@ def parse():
                     help="skip the CPU baseline leg (used for profiler passes)")
     ap.add_argument("--profile-case", action="store_true",
                     help="one untimed device decode of the workload, for ncu captures")
+    ap.add_argument("--workload", choices=["batch", "stream"], default="batch",
+                    help="batch: config 4 (default); stream: config 5")
+    ap.add_argument("--layers", action="store_true",
+                    help="print the per-layer table of one decode instead of the bench line")
+    ap.add_argument("--traffic-from", default=None,
+                    help="ncu CSV with dram__bytes_{read,write}.sum of conv_tc_tn_kernel launches")
     return ap.parse_args()
 
 
@@ -63,8 +78,14 @@ def lpt_shards(T, n):
     return [sorted(s) for s in shards]
 
 
-def workload(n_gpus):
-    T, zs = pt_b200.config4(seed=3, n=PER_GPU_REQUESTS * n_gpus)
+PER_GPU_STREAMS = 512
+
+
+def workload(n_gpus, kind="batch"):
+    if kind == "stream":
+        T, zs = pt_b200.config5(seed=4, n=PER_GPU_STREAMS * n_gpus)
+    else:
+        T, zs = pt_b200.config4(seed=3, n=PER_GPU_REQUESTS * n_gpus)
     w, _ = pt_b200.config3(seed=2)
     return T, zs, w
 
@@ -73,7 +94,26 @@ def audio_seconds(frames):
     return frames * HOP / SAMPLE_RATE
 
 
-def config_dict(n_gpus, T):
+def config_dict(n_gpus, T, kind="batch"):
+    if kind == "stream":
+        plan = pt_b200.stream_plan(T, pt_b200.STREAM_WIN, pt_b200.STREAM_CTX, exact=True)
+        executed = int(plan[:, 0].sum())
+        return {
+            "workload": "BASELINE config 5: 512 concurrent streams per GPU, T~U{100..1000} frames "
+                        "(seed 4), 64-frame windows with 16 frames of context per side (step 32), "
+                        "stitched; exact scheme (context widened to the 25/24-frame receptive "
+                        "radius: output equals a whole-utterance decode); config-3 decoder, "
+                        "random-init weights (seed 2); streams sharded whole across GPUs (LPT)",
+            "streams": len(T),
+            "frames": int(sum(T)),
+            "audio_s": round(audio_seconds(sum(T)), 3),
+            "windows": int(len(plan)),
+            "frames_executed": executed,
+            "recompute_factor": round(executed / max(1, int(sum(T))), 3),
+            "gflop_per_step_executed": round(sum(pt_b200.decoder_gflop(int(t)) for t in plan[:, 0]), 3),
+            "l2": "flushed between timed iterations (256 MiB device write)",
+            "parallelism": f"stream-parallel x{n_gpus}, no collective",
+        }
     return {
         "workload": "BASELINE config 4: 64 concurrent decoder requests per GPU, T~U{50..600} "
                     "frames (seed 3), config-3 v21_mbistft_16k decoder, random-init weights "
@@ -158,6 +198,69 @@ def traffic_from_profiles(kernel, flops_per_launch):
         return None
 
 
+def traffic_from_csv(path):
+    """profiles/conv_tc_traffic.json from an ncu CSV of conv_tc_tn_kernel launches of one
+    `--profile-case` decode (metrics dram__bytes_read.sum, dram__bytes_write.sum): total DRAM
+    bytes against the same launches' algorithmic FLOPs, so bench lines can scale it per launch."""
+    import csv
+    rows = list(csv.reader(open(path)))
+    hi = next(i for i, r in enumerate(rows) if "Kernel Name" in r and "Metric Name" in r)
+    h = rows[hi]
+    per = {}
+    for r in rows[hi + 1:]:
+        if len(r) != len(h):
+            continue
+        d = dict(zip(h, r))
+        if "conv_tc_tn_kernel" not in d["Kernel Name"]:
+            continue
+        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(d["Metric Unit"], None)
+        if d["Metric Name"].startswith("dram__bytes") and scale:
+            per.setdefault(d["ID"], 0.0)
+            per[d["ID"]] += float(d["Metric Value"].replace(",", "")) * scale
+    T, _, _ = workload(1)
+    flops = 1e9 * sum(pt_b200.conv_gflop(t) for t in T)
+    out = {"conv_tc_tn_kernel": {"dram_bytes": sum(per.values()), "flops": flops,
+                                 "launches": len(per), "workload": "bench.py --profile-case "
+                                 "(config 4, one decode)", "source": os.path.basename(path)}}
+    with open(os.path.join(REPO, "profiles", "conv_tc_traffic.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print(json.dumps(out))
+    return 0
+
+
+LAYER_NAMES = (["stage", "conv_pre", "ups.0"]
+               + [f"L1 rb{r} {c}.{j}" for r in range(3) for j in range(3) for c in ("convs1", "convs2")]
+               + ["ups.1"]
+               + [f"L2 rb{r} {c}.{j}" for r in range(3, 6) for j in range(3) for c in ("convs1", "convs2")]
+               + ["conv_post", "tail"])
+
+
+def layer_table(recs, steps):
+    """Markdown table of one decode's launches averaged over `steps` decodes: time, algorithmic
+    TFLOP/s and GB/s, and which roofline bounds the layer (FLOP/B against the ridge point of the
+    measured TF32 and HBM peaks)."""
+    peaks, src = measured_peaks()
+    tf = peaks["bf16_tflops_sustained"] / 2.0 * 1e12
+    bw = peaks["hbm_gbs"] * 1e9
+    lines = [f"peaks ({src}): TF32 {tf / 1e12:.1f} TFLOP/s, HBM {bw / 1e9:.0f} GB/s, "
+             f"ridge {tf / bw:.0f} FLOP/B",
+             "| layer | kernel | us | TFLOP/s | GB/s | FLOP/B | bound | roofline us | of roofline |",
+             "|---|---|---:|---:|---:|---:|---|---:|---:|"]
+    tot = 0.0
+    for i, (kind, bn, ms, fl, by) in enumerate(recs):
+        ms /= steps
+        tot += ms
+        name = LAYER_NAMES[i] if i < len(LAYER_NAMES) else str(i)
+        t = ms / 1e3
+        ai = fl / by if by else 0.0
+        bound = "tensor" if ai > tf / bw else "hbm"
+        roof = max(fl / tf, by / bw)
+        lines.append(f"| {name} | {kind} | {ms * 1e3:.1f} | {fl / t / 1e12:.1f} | {by / t / 1e9:.0f} | "
+                     f"{ai:.0f} | {bound} | {roof * 1e6:.1f} | {roof / t:.2f} |")
+    lines.append(f"| total | | {tot * 1e3:.1f} | | | | | | |")
+    return "\n".join(lines)
+
+
 # ----------------------------------------------------------------------------------------------
 def cpu_reference_sample(T, zs, w, threads):
     """Bounded sample for the reference CPU decoder: one request per host thread, taken from the
@@ -232,6 +335,8 @@ def reference_arm(args):
 # ----------------------------------------------------------------------------------------------
 def main():
     args = parse()
+    if args.traffic_from:
+        return traffic_from_csv(args.traffic_from)
     if args.impl == "reference":
         return reference_arm(args)
     import torch
@@ -247,7 +352,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
 
-    T_all, zs_all, w = workload(world)
+    kind = args.workload
+    T_all, zs_all, w = workload(world, kind)
     shard = lpt_shards(T_all, world)[rank]
     T = np.array([T_all[i] for i in shard], np.int64)
     zcat = np.concatenate([zs_all[i].ravel() for i in shard])
@@ -258,10 +364,35 @@ def main():
     wav_dev = torch.empty(int(HOP * T.sum()), device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > L2
 
+    def step_device():
+        if kind == "stream":
+            dec.stream_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), pt_b200.STREAM_WIN,
+                              pt_b200.STREAM_CTX, True, 0, sh)
+        else:
+            dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+
     if args.profile_case:
-        dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+        step_device()
         dec.sync(sh)
         print(json.dumps({"profile_case": True, "requests": len(T), "frames": int(T.sum())}))
+        return 0
+
+    if args.layers:
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_device()
+            dec.sync(sh)
+            dec.profile(True)
+            acc = None
+            for _ in range(max(args.steps, 1)):
+                flush.fill_(1.0)
+                step_device()
+                dec.sync(sh)
+                lt = dec.launch_times()
+                acc = lt if acc is None else [(a[0], a[1], a[2] + b[2], a[3], a[4])
+                                              for a, b in zip(acc, lt)]
+        print(layer_table(acc, max(args.steps, 1)))
+        dec.close()
         return 0
 
     def barrier():
@@ -279,7 +410,7 @@ def main():
     # ---- device-resident throughput ----------------------------------------------------------
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+            step_device()
         dec.sync(sh)
     dec.profile(True)
     clocks = ClockSampler()
@@ -294,7 +425,7 @@ def main():
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            dec.decode_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), sh)
+            step_device()
             e1.record(stream)
             dec.sync(sh)
             total_ms += e0.elapsed_time(e1)
@@ -307,7 +438,18 @@ def main():
     # ---- end to end through the host entry point (pinned buffers, copies timed) --------------
     z_host = torch.from_numpy(zcat).pin_memory()
     wav_host = torch.empty(int(HOP * T.sum()), dtype=torch.float32).pin_memory()
-    dec.decode_host_ptr(T, z_host.data_ptr(), wav_host.data_ptr(), sh)   # warm-up
+    def step_host():
+        if kind == "stream":
+            # the stream entry point works on device buffers: the copies are part of the step
+            z_dev.copy_(z_host, non_blocking=True)
+            step_device()
+            wav_host.copy_(wav_dev, non_blocking=True)
+            dec.sync(sh)
+        else:
+            dec.decode_host_ptr(T, z_host.data_ptr(), wav_host.data_ptr(), sh)
+
+    with torch.cuda.stream(stream):
+        step_host()   # warm-up
     barrier()
     e2e_ms = 0.0
     for _ in range(args.steps):
@@ -316,7 +458,8 @@ def main():
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        dec.decode_host_ptr(T, z_host.data_ptr(), wav_host.data_ptr(), sh)
+        with torch.cuda.stream(stream):
+            step_host()
         e1.record(stream)
         stream.synchronize()
         e2e_ms += e0.elapsed_time(e1)
@@ -334,9 +477,9 @@ def main():
     audio = audio_seconds(sum(T_all))
     # roofline of the dominant kernel instance, from the live per-launch events
     groups = {}
-    for kind, bn, ms, fl, by in launches:
+    for lkind, bn, ms, fl, by in launches:
         name = ("conv_tc_tn_kernel" if bn == 128 else f"conv_tc_win_kernel<{bn}>") if bn \
-            else f"{kind}_kernel"
+            else f"{lkind}_kernel"
         g = groups.setdefault(name, [0.0, 0.0, 0.0, 0])
         g[0] += ms
         g[1] += fl
@@ -374,7 +517,7 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "tf32 (tensor-core operands, round-to-nearest), fp32 accumulate/epilogues",
         "data": "synthetic (seeded N(0,1) latents, N(0,0.02^2) weights)",
-        "config": config_dict(world, T_all),
+        "config": config_dict(world, T_all, kind),
         "conv_tflops": round(conv_tflops, 1),
         "conv_tf32_frac": round(conv_tflops / tf32_peak, 4),
         "roofline": roof,
@@ -385,7 +528,9 @@ def main():
         "gpu_launches": int(gpu_launches),
         "clocks": clk,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if kind == "stream":
+        out["roofline"]["note"] = "launch records of the last decode pass of a step"
+    if world == 1 and not args.no_cpu_baseline and kind == "batch":
         out["cpu_baseline"] = cpu_baseline_block(T_all, zs_all, w)
     dec.close()
     print(json.dumps(out))

@@ -405,7 +405,9 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
           const float *in = j == 0 ? d->LU[s] : d->XT[s];
           if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e)) return -1;
         }
-        rec(d, st, LK_CONV, cflops(fout, C, C, K), fout * 4 * C * 4, d->rb2[r][j].bn);
+        // convs2 bytes: input + residual + outputs (+ the branch sum read by resblocks 1, 2)
+        const int nio = j < 2 ? 4 : rb == 0 ? 3 : 4;
+        rec(d, st, LK_CONV, cflops(fout, C, C, K), fout * nio * C * 4, d->rb2[r][j].bn);
         {  // convs2.j + residual (+ leaky for the next stage / branch sum)
           EpiParams e = rows_epi(mk, C);
           e.res = j == 0 ? d->U[s] : d->XB[s];
