@@ -53,8 +53,15 @@ struct TailArgs {
 __device__ __forceinline__ float tr_exp(float x, bool f32) { return f32 ? expf(x) : (float)exp((double)x); }
 __device__ __forceinline__ float tr_sin(float x, bool f32) { return f32 ? sinf(x) : (float)sin((double)x); }
 __device__ __forceinline__ float tr_cos(float x, bool f32) { return f32 ? cosf(x) : (float)cos((double)x); }
+// magnitude / phase of one bin: re = exp(a) * cos(pi * sin(b)), im = exp(a) * sin(pi * sin(b))
+__device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, float &iv) {
+  const float mag = tr_exp(la, f32);
+  const float ph = __fmul_rn(tr_sin(lb, f32), 3.1415927410125732f);
+  rv = __fmul_rn(mag, tr_cos(ph, f32));
+  iv = __fmul_rn(mag, tr_sin(ph, f32));
+}
 
-__global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
+__global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a) {
   extern __shared__ __align__(16) unsigned char tail_smem[];
   TailSmem &S = *reinterpret_cast<TailSmem *>(tail_smem);
   auto &re = S.re;
@@ -95,34 +102,58 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   const long long F0 = ((m_lo + 8) >> 2) - 3;
   const int NF = (int)(((m_hi + 8) >> 2) - F0 + 1);
 
-  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im
-  for (int it = threadIdx.x; it < NF * 36; it += blockDim.x) {
+  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im; two bins a thread at a time
+  // (independent chains in flight).  Frames outside [0, Tp) never reach the overlap-add: zeros.
+  for (int it = threadIdx.x; it < NF * 36; it += 2 * blockDim.x) {
+    const int it2 = it + blockDim.x;
     const int fl = it / 36, rb = it - fl * 36, b = rb / 9, k = rb - b * 9;
-    const long long f = F0 + fl;
-    float rv = 0.0f, iv = 0.0f;   // frames outside [0, Tp) never reach the overlap-add
-    if (f >= 0 && f < Tp) {
+    const int fl2 = it2 / 36, rb2 = it2 - fl2 * 36, b2 = rb2 / 9, k2 = rb2 - b2 * 9;
+    const long long f = F0 + fl, f2 = F0 + fl2;
+    const bool v1 = f >= 0 && f < Tp, v2 = it2 < NF * 36 && f2 >= 0 && f2 < Tp;
+    float la = 0.0f, lb = 0.0f, la2 = 0.0f, lb2 = 0.0f;
+    if (v1) {
       const float *pf = post + f * a.st_t;
-      const float mag = tr_exp(pf[(long long)(b * 18 + k) * a.st_c], f32);
-      const float ph = __fmul_rn(tr_sin(pf[(long long)(b * 18 + 9 + k) * a.st_c], f32),
-                                 3.1415927410125732f);
-      rv = __fmul_rn(mag, tr_cos(ph, f32));
-      iv = __fmul_rn(mag, tr_sin(ph, f32));
+      la = pf[(long long)(b * 18 + k) * a.st_c];
+      lb = pf[(long long)(b * 18 + 9 + k) * a.st_c];
     }
-    re[fl][b][k] = (double)rv;
-    im[fl][b][k] = (double)iv;
+    if (v2) {
+      const float *pf = post + f2 * a.st_t;
+      la2 = pf[(long long)(b2 * 18 + k2) * a.st_c];
+      lb2 = pf[(long long)(b2 * 18 + 9 + k2) * a.st_c];
+    }
+    float rv, iv, rv2, iv2;
+    tr_bin(la, lb, f32, rv, iv);
+    tr_bin(la2, lb2, f32, rv2, iv2);
+    re[fl][b][k] = v1 ? (double)rv : 0.0;
+    im[fl][b][k] = v1 ? (double)iv : 0.0;
+    if (it2 < NF * 36) {
+      re[fl2][b2][k2] = v2 ? (double)rv2 : 0.0;
+      im[fl2][b2][k2] = v2 ? (double)iv2 : 0.0;
+    }
   }
   __syncthreads();
   // ---- 1b. per (frame, band, output bin): the 9 -> 16 basis sums in double, then the window
   static_assert(kTailThreads % 16 == 0, "phase 1b keeps n = threadIdx.x % 16");
-  for (int it = threadIdx.x; it < NF * 64; it += blockDim.x) {
+  // two (frame, band) items a thread at a time: four independent double chains in flight
+  for (int it = threadIdx.x; it < NF * 64; it += 2 * blockDim.x) {
+    const int it2 = it + blockDim.x;
+    const bool two = it2 < NF * 64;
     const int fl = it >> 6, b = (it >> 4) & 3;
-    double er = 0.0, ei = 0.0;
+    const int fl2 = two ? it2 >> 6 : fl, b2 = (it2 >> 4) & 3;
+    double er = 0.0, ei = 0.0, er2 = 0.0, ei2 = 0.0;
 #pragma unroll
     for (int k = 0; k < 9; ++k) {   // zero basis entries are skipped, as in the reference einsum
-      if (bcn[k] != 0.0) er = __dadd_rn(er, __dmul_rn(bcn[k], re[fl][b][k]));
-      if (bsn[k] != 0.0) ei = __dadd_rn(ei, __dmul_rn(bsn[k], im[fl][b][k]));
+      if (bcn[k] != 0.0) {
+        er = __dadd_rn(er, __dmul_rn(bcn[k], re[fl][b][k]));
+        er2 = __dadd_rn(er2, __dmul_rn(bcn[k], re[fl2][b2][k]));
+      }
+      if (bsn[k] != 0.0) {
+        ei = __dadd_rn(ei, __dmul_rn(bsn[k], im[fl][b][k]));
+        ei2 = __dadd_rn(ei2, __dmul_rn(bsn[k], im[fl2][b2][k]));
+      }
     }
     fr[fl][b * 16 + n] = __fmul_rn(__fadd_rn((float)er, (float)ei), wn);
+    if (two) fr[fl2][b2 * 16 + n] = __fmul_rn(__fadd_rn((float)er2, (float)ei2), wn);
   }
   __syncthreads();
 
@@ -144,8 +175,9 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
       }
     }
     const float ec = env > 1e-9f ? env : 1e-9f;
-    sm[ml] = make_float4(__fdiv_rn(ola[0], ec), __fdiv_rn(ola[1], ec), __fdiv_rn(ola[2], ec),
-                         __fdiv_rn(ola[3], ec));
+    // stored with the zero-stuffing gain 4 applied (a power of two: exact), as phase 3 uses it
+    sm[ml] = make_float4(__fmul_rn(4.0f, __fdiv_rn(ola[0], ec)), __fmul_rn(4.0f, __fdiv_rn(ola[1], ec)),
+                         __fmul_rn(4.0f, __fdiv_rn(ola[2], ec)), __fmul_rn(4.0f, __fdiv_rn(ola[3], ec)));
   }
   __syncthreads();
 
@@ -154,27 +186,32 @@ __global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   const int jn = (int)(nwav - j0 < kTailW ? nwav - j0 : kTailW);
   const int mlo = (int)m_lo, nw = (int)nwav, jb = (int)j0;
   const int klo = (int)keep_lo, khi = (int)(keep_hi < nwav ? keep_hi : nwav);
-  for (int jj = threadIdx.x; jj < jn; jj += blockDim.x) {
-    const int j = jb + jj;
-    if (j < klo || j >= khi) continue;
-    float acc = 0.0f;
-    const int k0 = (31 - j) & 3;  // first tap with (j + k - 31) % 4 == 0
+  // four outputs a thread, 256 apart: they share the tap phase k0 and every filter tap load, and
+  // keep four independent accumulation chains in flight; each output sums tap-major then band
+  static_assert(kTailW == 4 * kTailThreads, "phase 3 gives every thread four outputs");
+  const int j = jb + threadIdx.x;
+  const int k0 = (31 - j) & 3;   // first tap with (j + k - 31) % 4 == 0 (same for j + 256u)
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 4
-    for (int k = k0; k < 63; k += 4) {
-      const int i = j + k - 31;
+  for (int k = k0; k < 63; k += 4) {
+    const float4 h4 = S.h[k];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = j + 256 * u + k - 31;
       if (i < 0 || i >= nw) continue;
-      const float4 s4 = sm[(i >> 2) - mlo];
-      const float4 h4 = S.h[k];
-      float x = __fmul_rn(4.0f, s4.x);
-      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.x, x));
-      x = __fmul_rn(4.0f, s4.y);
-      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.y, x));
-      x = __fmul_rn(4.0f, s4.z);
-      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.z, x));
-      x = __fmul_rn(4.0f, s4.w);
-      if (x != 0.0f) acc = __fadd_rn(acc, __fmul_rn(h4.w, x));
+      const float4 x4 = sm[(i >> 2) - mlo];
+      float t = acc[u];
+      if (x4.x != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.x, x4.x));
+      if (x4.y != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.y, x4.y));
+      if (x4.z != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.z, x4.z));
+      if (x4.w != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.w, x4.w));
+      acc[u] = t;
     }
-    wav[j] = acc;
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int jj = threadIdx.x + 256 * u, ju = j + 256 * u;
+    if (jj < jn && ju >= klo && ju < khi) wav[ju] = acc[u];
   }
 }
 
