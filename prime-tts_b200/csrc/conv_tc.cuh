@@ -896,11 +896,11 @@ struct TNCfg {
 };
 
 // Instances whose outputs leave through TMA tile stores staged in shared memory: the rows-mode
-// decoder epilogues except the one that also writes the reflection row (that row lies in a gap
-// that the staged stores of its neighbours would zero).
+// decoder epilogues.  The reflection-row instance stages the mirrored value into the target gap
+// row (mask bit 2), which the decoder layout keeps in the same 16-row pass as its source.
 template <int MODE, int F>
 struct TNTmaStore {
-  static constexpr bool value = MODE == EPI_ROWS && F != EF_GENERIC && (F & EF_REFL) == 0;
+  static constexpr bool value = MODE == EPI_ROWS && F != EF_GENERIC;
 };
 
 // Plain-mode (interpreter ABI) epilogue of one 32-channel x 32-row block: this thread's channel
@@ -1023,16 +1023,39 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
     __syncwarp();
     const uint32_t s0 = stage + (two ? 0u : static_cast<uint32_t>(slot) * (16 * kBK * 4));
     const uint32_t s1 = two ? stage + 16 * kBK * 4 : s0;
+    if constexpr ((F & EF_REFL) != 0) {
+      // out1 only: rows whose mask has bit 2 take the value of the row two below (same pass)
+      const unsigned tg = (__ballot_sync(0xffffffffu, (mk >> 2) & 1u) >> (16 * h)) & 0xffffu;
+      float wv[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const bool ok = ((vh >> i) & 1) && colok;
-      float x = v[i] + bias;
-      if (hr) x += rs[i];
-      if (am == 2) x = ac[i] + x;
-      else if (am == 3) x = (ac[i] + x) / 3.0f;
-      const uint32_t at = static_cast<uint32_t>(i * kBK * 4 + lane * 4);
-      if (o0) st_shared_f32(s0 + at, ok ? x : 0.0f);
-      if (o1) st_shared_f32(s1 + at, ok ? tf32_rna(leaky(x, e.alpha1)) : 0.0f);
+      for (int i = 0; i < 16; ++i) {
+        float x = v[i] + bias;
+        if (hr) x += rs[i];
+        if (am == 2) x = ac[i] + x;
+        else if (am == 3) x = (ac[i] + x) / 3.0f;
+        wv[i] = tf32_rna(leaky(x, e.alpha1));
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float val = 0.0f;
+        if (colok) {
+          if ((vh >> i) & 1) val = wv[i];
+          else if (i + 2 < 16 && ((tg >> i) & 1)) val = wv[i + 2 < 16 ? i + 2 : i];
+        }
+        st_shared_f32(s1 + static_cast<uint32_t>(i * kBK * 4 + lane * 4), val);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const bool ok = ((vh >> i) & 1) && colok;
+        float x = v[i] + bias;
+        if (hr) x += rs[i];
+        if (am == 2) x = ac[i] + x;
+        else if (am == 3) x = (ac[i] + x) / 3.0f;
+        const uint32_t at = static_cast<uint32_t>(i * kBK * 4 + lane * 4);
+        if (o0) st_shared_f32(s0 + at, ok ? x : 0.0f);
+        if (o1) st_shared_f32(s1 + at, ok ? tf32_rna(leaky(x, e.alpha1)) : 0.0f);
+      }
     }
     fence_proxy_async_smem();
     __syncwarp();

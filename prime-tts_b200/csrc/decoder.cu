@@ -2,10 +2,10 @@
 //
 // Ragged batch layout.  At each time resolution (level 0: latent frames T, level 1: 4T after
 // ups.0, level 2: 16T after ups.1) the requests are stacked along time in one channels-last
-// tensor [rows][C], each request's rows preceded and followed by zero gap rows: kGap[0] = 8 at
-// level 0 (conv_pre reaches 3 rows, ups.0 reads 2 before and 1 after a request) and kGap[1..2] = 28
-// at levels 1 and 2 (the widest conv reaches dilation 5 x (11-1)/2 = 25 rows; conv_post reads
-// 3 + 1 reflection row).  So one launch per layer computes every request exactly as if it ran
+// tensor [rows][C], each request's rows preceded and followed by zero gap rows: 8 at level 0
+// (conv_pre reaches 3 rows, ups.0 reads 2 before and 1 after a request), 28 at level 1 and 32 at
+// level 2 (the widest conv reaches dilation 5 x (11-1)/2 = 25 rows; conv_post reads 3 + 1
+// reflection row).  So one launch per layer computes every request exactly as if it ran
 // alone: the zero gap rows are the convolutions' zero padding, and the epilogue never writes them
 // (a per-row mask), so they stay zero.
 //
@@ -37,7 +37,11 @@ using namespace ptb;
 
 namespace {
 
-constexpr int64_t kGap[3] = {8, 28, 28};
+constexpr int64_t kGap[3] = {8, 28, 32};
+// rows before the first request; level 2 starts every request at a row = 4 (mod 16) (a lead of
+// 36, gaps of 32, request lengths 16T), so a request's reflection row (-1) and its source (+1)
+// fall in the same 16-row epilogue pass
+constexpr int64_t kLead[3] = {8, 28, 36};
 // receptive radius of one output sample, in latent frames before / after its own frame
 // (PQMF 63 taps, overlap-add, conv_post k7, two MRF blocks reaching 60 rows, two k16/s4 convT,
 // conv_pre k7, propagated back to the latent)
@@ -184,13 +188,15 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
   const int64_t scale[3] = {1, 4, 16};
   std::vector<int64_t> a[3];
   for (int l = 0; l < 3; ++l) {
-    int64_t off = kGap[l];
+    int64_t off = kLead[l];
     for (int i = 0; i < nreq; ++i) {
       a[l].push_back(off);
       off += scale[l] * T[i] + kGap[l];
     }
     p.R[l] = off;
   }
+  for (int i = 0; i < nreq; ++i)
+    PTB_REQUIRE(a[2][i] % 16 == 4, "pt_b200: level-2 layout broke the reflection-row alignment");
   for (int i = 0; i < nreq; ++i) {
     p.max_T = T[i] > p.max_T ? T[i] : p.max_T;
     p.total_z += 192 * T[i];
@@ -210,7 +216,10 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
   mr = m[2];
   mp.assign((size_t)p.R[2], 0);
   for (int i = 0; i < nreq; ++i) {
-    mr[(size_t)a[2][i] + 1] |= 2;  // local row 1 is mirrored into row -1 (reflection pad (1,0))
+    // reflection pad (1,0): local row 1 (bit 1 on the source) is mirrored into row -1 (bit 2 on
+    // the target, a gap row)
+    mr[(size_t)a[2][i] + 1] |= 2;
+    mr[(size_t)a[2][i] - 1] |= 4;
     std::memset(mp.data() + a[2][i] - 1, 1, (size_t)(16 * T[i] + 1));
   }
   std::vector<int> ob01((size_t)p.R[0], INT_MIN), ob12((size_t)p.R[1], INT_MIN);
