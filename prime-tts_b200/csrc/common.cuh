@@ -36,6 +36,7 @@ const char *last_error();
 // counts this library's kernel launches on the calling thread (reported by
 // pt_b200_kernel_launches and by bench.py as gpu_launches)
 void count_launch(long n = 1);
+long launches(int reset);
 
 inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 

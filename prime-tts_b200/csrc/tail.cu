@@ -272,6 +272,9 @@ static int tail_ready() {
   return 0;
 }
 
+// constants on the calling thread's current device (call before a stream capture)
+int tail_prepare() { return tail_ready(); }
+
 // single request, channel-major post [72][Tp]
 int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wav_dev,
              cudaStream_t st) {
