@@ -295,6 +295,22 @@ PT_B200_API int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstr
                                       const int64_t *T, const float *z_dev, int win, int ctx,
                                       int exact, int64_t max_frames, float *wav_dev);
 
+/* ---- Weight container (extension) ------------------------------------------------------
+ * The reference ships its weights in one .ptk container (tools/export_v21.py:1-40: header
+ * <IIIiq> "PTK1", 136-byte records <64si4x6qqq>, 64-byte aligned payloads, fp16 for names ending
+ * in "#h"), read by its runtime at start-up.  These read the decoder's records
+ * (dec.conv_pre, dec.ups.{0,1}, dec.resblocks.{0..5}.convs{1,2}.{0..2}, dec.subband_conv_post,
+ * and the PQMF synthesis filter dec.Conv) into pt_b200_dec_weights, fp16 payloads widened to
+ * fp32 (exact; fp16 values are exact in TF32 too).  No GPU is needed to read a container.
+ * pt_b200_ptk_open returns NULL (message in pt_b200_last_error) on a missing file, bad magic,
+ * missing tensor or wrong size.  The weight pointers stay valid until pt_b200_ptk_close. */
+typedef struct pt_b200_ptk pt_b200_ptk;
+PT_B200_API pt_b200_ptk *pt_b200_ptk_open(const char *path);
+PT_B200_API int pt_b200_ptk_decoder_weights(const pt_b200_ptk *k, pt_b200_dec_weights *w);
+PT_B200_API void pt_b200_ptk_close(pt_b200_ptk *k);
+/* Open, create the decoder on `device`, close. */
+PT_B200_API pt_b200_decoder *pt_b200_decoder_create_from_ptk(int device, const char *path);
+
 /* Conv1d with no device allocation (no counterpart in the reference).  For callers that cannot
  * call cudaMalloc/cudaFree: hosts that own every device allocation (pooled or framework
  * allocators), real-time threads that must not take the allocator's locks, processes whose

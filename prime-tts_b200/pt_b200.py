@@ -139,6 +139,10 @@ _SIGS = {
     "pt_b200_conv_noalloc": ([C.c_int, C.c_void_p, C.c_void_p, _i64, _i64, _i64, C.c_void_p,
                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                               C.c_int, C.c_float], C.c_int),
+    "pt_b200_ptk_open": ([C.c_char_p], C.c_void_p),
+    "pt_b200_ptk_decoder_weights": ([C.c_void_p, C.POINTER(DecWeightsC)], C.c_int),
+    "pt_b200_ptk_close": ([C.c_void_p], None),
+    "pt_b200_decoder_create_from_ptk": ([C.c_int, C.c_char_p], C.c_void_p),
     "pt_b200_last_error": ([], C.c_char_p),
     "pt_b200_kernel_launches": ([C.c_int], C.c_long),
 }
@@ -382,6 +386,51 @@ def make_decoder_weights(rng: np.random.Generator, wstd: float = 0.02,
                           pqmf_synthesis_filter())
 
 
+def _conv_sizes():
+    """Packed element counts of every decoder record, in DecoderWeights order."""
+    n = {"pre_w": 512 * 7 * 192, "pre_b": 512, "post_w": 72 * 7 * 128, "post_b": 72}
+    for s, (cin, c) in enumerate(((512, 256), (256, 128))):
+        n[f"ups_w{s}"] = 4 * c * 4 * cin
+        n[f"ups_b{s}"] = c
+        for rb in range(3):
+            K = RB_KERNELS[rb]
+            n[f"rb{3 * s + rb}"] = (c * K * c, c)
+    return n
+
+
+def load_ptk(path: str) -> DecoderWeights:
+    """Decoder weights read from a reference weight container (.ptk) by the library's reader
+    (pt_b200_ptk_open: fp16 '#h' payloads widened to fp32; no GPU needed)."""
+    h = lib().pt_b200_ptk_open(path.encode())
+    if not h:
+        raise PtB200Error(f"pt_b200_ptk_open: {lib().pt_b200_last_error().decode()}")
+    try:
+        cw = DecWeightsC()
+        _check(lib().pt_b200_ptk_decoder_weights(h, C.byref(cw)), "pt_b200_ptk_decoder_weights")
+        n = _conv_sizes()
+
+        def arr(ptr, count):
+            return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), (count,)).copy()
+
+        rb_w1 = [[None] * 3 for _ in range(6)]
+        rb_b1 = [[None] * 3 for _ in range(6)]
+        rb_w2 = [[None] * 3 for _ in range(6)]
+        rb_b2 = [[None] * 3 for _ in range(6)]
+        for r in range(6):
+            wn, bn = n[f"rb{r}"]
+            for j in range(3):
+                rb_w1[r][j], rb_b1[r][j] = arr(cw.rb_w1[r][j], wn), arr(cw.rb_b1[r][j], bn)
+                rb_w2[r][j], rb_b2[r][j] = arr(cw.rb_w2[r][j], wn), arr(cw.rb_b2[r][j], bn)
+        return DecoderWeights(arr(cw.pre_w, n["pre_w"]), arr(cw.pre_b, n["pre_b"]),
+                              [arr(cw.ups_w[s], n[f"ups_w{s}"]) for s in range(2)],
+                              [arr(cw.ups_b[s], n[f"ups_b{s}"]) for s in range(2)],
+                              rb_w1, rb_b1, rb_w2, rb_b2,
+                              arr(cw.post_w, n["post_w"]), arr(cw.post_b, n["post_b"]),
+                              arr(cw.pqmf, 4 * 63).reshape(1, 4, 63))
+    finally:
+        lib().pt_b200_ptk_close(h)
+
+
 def config3(seed: int = 2, T: int = 226):
     """Config 3: latent z [192][T] ~ N(0,1), then the decoder weights, from one generator."""
     rng = np.random.default_rng(seed)
@@ -459,6 +508,11 @@ class Decoder:
             raise PtB200Error(f"pt_b200_decoder_create failed: {lib().pt_b200_last_error()}")
         self.h = h
         self.device = device
+
+    @classmethod
+    def from_container(cls, path: str, device: int = 0) -> "Decoder":
+        """The decoder of a reference weight container (.ptk)."""
+        return cls(load_ptk(path), device)
 
     def close(self) -> None:
         if self.h:

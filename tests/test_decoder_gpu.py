@@ -137,3 +137,30 @@ def test_graph_replay_is_bitwise_and_counts_launches(dec):
     assert counts[0] > 0 and all(c == counts[0] for c in counts), counts
     ref = dec.decode(zs)   # host entry point, separate buffers: its own eager decode
     np.testing.assert_array_equal(np.concatenate(ref), outs[0])
+
+
+def test_decoder_from_container(tmp_path, orc):
+    """A decoder created from a reference weight container (.ptk, fp16 conv weights) matches the
+    oracle run on the same fp16-rounded weights; the one-call C entry gives the same bits."""
+    import ctypes as C
+    from ptk_writer import decoder_tensors, fp16_rounded, write_ptk
+    w, z = pt_b200.config3(seed=2, T=120)
+    path = str(tmp_path / "dec.ptk")
+    write_ptk(path, decoder_tensors(w))
+    d = pt_b200.Decoder.from_container(path)
+    got = d.decode([z])[0]
+    d.close()
+    m = oracle.metrics(got, orc.decode(fp16_rounded(w), z))
+    assert m["sndr_db"] >= 60.0, m
+    h = pt_b200.lib().pt_b200_decoder_create_from_ptk(0, path.encode())
+    assert h
+    try:
+        T = np.array([z.shape[1]], np.int64)
+        zc = np.ascontiguousarray(z, np.float32)
+        wav = np.empty(256 * z.shape[1], np.float32)
+        rc = pt_b200.lib().pt_b200_decode_batch(h, None, 1, T.ctypes.data_as(C.POINTER(C.c_int64)),
+                                                zc.ctypes.data, wav.ctypes.data)
+        assert rc == 0
+        np.testing.assert_array_equal(wav, got)
+    finally:
+        pt_b200.lib().pt_b200_decoder_destroy(h)
