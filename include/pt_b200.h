@@ -295,6 +295,45 @@ PT_B200_API int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstr
                                       const int64_t *T, const float *z_dev, int win, int ctx,
                                       int exact, int64_t max_frames, float *wav_dev);
 
+/* ---- Streaming with carried state (extension) --------------------------------------------
+ * The same streams decoded chunk by chunk without recomputing any frame: pass k feeds latent
+ * frames [k*chunk, (k+1)*chunk) of every stream still running, and every layer computes only
+ * the rows whose inputs are now complete, reading the rows it needs from earlier passes out of
+ * the session's activations (the carried state).  Each pass emits the output samples whose
+ * receptive field is complete (24 latent frames of look-ahead; a stream's last pass flushes
+ * it), bit-identical to the whole-utterance decode.  This replaces the reference's re-run of
+ * the decoder on overlapping windows (pt_v21_stream_chunk, runtime/v21/src/pt_v21_host.c:
+ * 2749-2912) where the windows were meant to cover the receptive field.
+ *
+ * A session holds the activations of its streams from their first frame: about 205 KB of
+ * device memory per latent frame of capacity (sum of T).  Latents are concatenated as for
+ * pt_b200_decode_batch_device ([192][T[i]] per stream); pass k reads only its own frames, so
+ * z_dev may be filled as frames arrive.  Output samples go to wav_dev at the stream's offset in
+ * the concatenated waveform (256*T[i] samples per stream). */
+typedef struct pt_b200_carry pt_b200_carry;
+/* Plan the passes and allocate the session on the decoder's device; NULL on error. */
+PT_B200_API pt_b200_carry *pt_b200_carry_open(pt_b200_decoder *d, int nstreams, const int64_t *T,
+                                             int chunk);
+PT_B200_API int pt_b200_carry_passes(const pt_b200_carry *c);
+/* Pass `pass` (0, 1, ... in order, each once) on `stream` (NULL: the decoder's stream),
+ * asynchronous; the status covers argument and launch errors (pt_b200_decoder_sync reports
+ * device errors). */
+PT_B200_API int pt_b200_carry_run(pt_b200_carry *c, void *stream, int pass, const float *z_dev,
+                                  float *wav_dev);
+/* Rewind to pass 0 for a new run of the same streams (new latents).  Nothing is cleared: every
+ * row a pass reads was written earlier in the same run, and gap rows only ever hold zeros. */
+PT_B200_API int pt_b200_carry_reset(pt_b200_carry *c);
+PT_B200_API void pt_b200_carry_close(pt_b200_carry *c);
+/* Open, run every pass, close. */
+PT_B200_API int pt_b200_stream_decode_carry(pt_b200_decoder *d, void *stream, int nstreams,
+                                            const int64_t *T, const float *z_dev, int chunk,
+                                            float *wav_dev);
+/* The pass plan alone (no GPU): returns the pass count (-1 on bad arguments or a plan that
+ * fails its own checks) and, when cap >= passes * nstreams, the samples [lo, hi) of each
+ * stream that each pass emits (index pass * nstreams + stream). */
+PT_B200_API int64_t pt_b200_carry_plan(int nstreams, const int64_t *T, int chunk, int64_t *lo,
+                                       int64_t *hi, int64_t cap);
+
 /* ---- Weight container (extension) ------------------------------------------------------
  * The reference ships its weights in one .ptk container (tools/export_v21.py:1-40: header
  * <IIIiq> "PTK1", 136-byte records <64si4x6qqq>, 64-byte aligned payloads, fp16 for names ending

@@ -239,8 +239,10 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
     if ((F & EF_OUT0) && make_map_out(&to0, L.e.out0, L.e.ldc, L.g.m_rows)) return -1;
     if ((F & EF_OUT1) && make_map_out(&to1, L.e.out1, L.e.ldc1, L.g.m_rows)) return -1;
   }
+  PTB_REQUIRE(!L.g.tiles || (L.batch == 1 && L.g.ntiles > 0),
+              "pt_b200: a conv tile list needs batch 1 and at least one tile");
   const long long tiles = (long long)((L.g.n_cols + kBM - 1) / kBM) *
-                          ((L.g.m_rows + kTNRows - 1) / kTNRows) * L.batch;
+                          (L.g.tiles ? L.g.ntiles : ((L.g.m_rows + kTNRows - 1) / kTNRows) * L.batch);
   ConvGeom g = L.g;
   g.nbatch = L.batch;
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
@@ -310,6 +312,10 @@ int launch_conv(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   if (no_pers < 0) no_pers = getenv("PT_B200_NO_PERSIST") ? atoi(getenv("PT_B200_NO_PERSIST")) : 0;
   static int no_tn = -1;
   if (no_tn < 0) no_tn = getenv("PT_B200_NO_TN") ? atoi(getenv("PT_B200_NO_TN")) : 0;
+  if (L.g.tiles) {   // tile lists exist only in the channels-on-M kernel
+    PTB_REQUIRE(L.bn == 128 && halo <= kWinHalo, "pt_b200: a conv tile list needs the channels-on-M kernel");
+    return launch_tn(L, gerr, st);
+  }
   if (!no_win && halo <= kWinHalo) {
     if (L.bn == 128) {
       if (!no_tn) return launch_tn(L, gerr, st);

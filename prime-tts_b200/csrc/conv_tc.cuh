@@ -43,6 +43,11 @@ struct ConvGeom {
   int row_step;   // activation row increment per tap
   int nkb;        // ntap * cin32 / 32
   int nbatch;     // batch items (the persistent kernel walks them in its tile list)
+  // Channels-on-M kernel only: an explicit tile list {first row, rows} (rows a multiple of 16,
+  // at most 256; batch 1), used instead of 256-row tiles over [0, m_rows) -- the streaming
+  // executor computes only each stream's newly computable rows of a layer.
+  const int2 *tiles;
+  int ntiles;
 };
 
 struct EpiParams {
@@ -898,16 +903,41 @@ struct TNCfg {
 // Instances whose outputs leave through TMA tile stores staged in shared memory: the rows-mode
 // decoder epilogues.  The reflection-row instance stages the mirrored value into the target gap
 // row (mask bit 2), which the decoder layout keeps in the same 16-row pass as its source.
+// Tile t of a channels-on-M launch: channel tile mi (fastest) of time tile t / mt -- a 256-row
+// slice of [0, m_rows) of batch item z, or entry t / mt of the launch's tile list.
+struct TNTile {
+  int z, mi, r0, nr;
+};
+__device__ __forceinline__ TNTile tn_tile(const ConvGeom &g, int t, int mt, int tt) {
+  TNTile x;
+  if (g.tiles) {
+    const int entry = t / mt;
+    const int2 v = g.tiles[entry];
+    x.z = 0;
+    x.mi = t - entry * mt;
+    x.r0 = v.x;
+    x.nr = v.y;
+  } else {
+    x.z = t / (mt * tt);
+    const int r = t - x.z * mt * tt, ti = r / mt;
+    x.mi = r - ti * mt;
+    x.r0 = ti * kTNRows;
+    x.nr = kTNRows;
+  }
+  return x;
+}
+
 template <int MODE, int F>
 struct TNTmaStore {
   static constexpr bool value = MODE == EPI_ROWS && F != EF_GENERIC;
 };
 
 // Plain-mode (interpreter ABI) epilogue of one 32-channel x 32-row block: this thread's channel
-// n, time rows t0..t0+31, read from TMEM at `taddr` (D[n][t0 + i] -> column i).
+// n, time rows t0..t0+31, read from TMEM at `taddr` (D[n][t0 + i] -> column i).  Rows at or past
+// `tend` (the tile's end, at most m_rows) are not stored.
 template <int MODE, int F>
 __device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z, int n, int t0,
-                                       int m_rows) {
+                                       int tend) {
   if constexpr (MODE == EPI_PLAIN_CONV || MODE == EPI_PLAIN_CONVT) {
     float v[32];
     tmem_ld32(taddr, v);
@@ -919,7 +949,7 @@ __device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int t = t0 + i;
-        if (t < e.tout) {
+        if (t < e.tout && t < tend) {
           float x = v[i] + bias;
           if (e.epi0) x = epi_op(x, e.epi0, e.a0);
           if (e.epi1) x = epi_op(x, e.epi1, e.a1);
@@ -933,7 +963,7 @@ __device__ __forceinline__ void tn_epi(const EpiParams &e, uint32_t taddr, int z
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int t = t0 + i;
-        if (t < m_rows) {
+        if (t < tend) {
           const long long oi = (e.q0 + t) * e.s + r - e.pad;
           if (oi >= 0 && oi < e.tout) {
             float x = v[i] + bias;
@@ -1122,11 +1152,10 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   const int kc = g.cin32 / kBK;
   const int span = (g.ntap - 1) * g.row_step;
   const int lo_off = span < 0 ? span : 0;
-  const int wrows = kTNRows + (span < 0 ? -span : span);
-  const int nbox = (wrows + kWinBox - 1) / kWinBox;
+  const int wspan = span < 0 ? -span : span;
   const int mt = (g.n_cols + kBM - 1) / kBM;              // channel tiles (fastest)
   const int tt = (g.m_rows + kTNRows - 1) / kTNRows;      // time tiles
-  const int ntiles = mt * tt * g.nbatch;
+  const int ntiles = g.tiles ? g.ntiles * mt : mt * tt * g.nbatch;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -1165,8 +1194,10 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       bool ok = true;
       int cw = 0, ca = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int z = t / (mt * tt), r = t - z * mt * tt, ti = r / mt, mi = r - ti * mt;
-        const int wlo = ti * kTNRows + g.row_off0 + lo_off;
+        const TNTile tl = tn_tile(g, t, mt, tt);
+        const int z = tl.z, mi = tl.mi;
+        const int wlo = tl.r0 + g.row_off0 + lo_off;
+        const int nbox = (tl.nr + wspan + kWinBox - 1) / kWinBox;
         for (int c = 0; c < kc && ok; ++c, ++cw) {
           const int ws = cw & 1;
           if (!mbar_wait(wempty(ws), ((cw >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
@@ -1209,11 +1240,11 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     }
   } else if (warp == 9) {
     if (lane == 0) {
-      // ---------------- MMA issuer: M = 128 channels, N = 256 time rows
-      const uint32_t idesc = idesc_tf32(kBM, kTNRows);
+      // ---------------- MMA issuer: M = 128 channels, N = the tile's time rows (<= 256)
       bool ok = true;
       int cw = 0, ca = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+        const uint32_t idesc = idesc_tf32(kBM, tn_tile(g, t, mt, tt).nr);
         const int ab = it & 1;
         if (!mbar_wait(aempty(ab), ((it >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
           ok = false;
@@ -1263,7 +1294,12 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int ab = it & 1;
-      const int z = t / (mt * tt), r = t - z * mt * tt, ti = r / mt, mi = r - ti * mt;
+      const TNTile tile = tn_tile(g, t, mt, tt);
+      const int z = tile.z, mi = tile.mi, r0 = tile.r0;
+      // this warp's 32-row blocks of the tile: half 0 takes the first ceil(nblk / 2)
+      const int nblk = (tile.nr + 31) / 32, bh = (nblk + 1) / 2;
+      const int b0 = half * bh, nb = half ? nblk - bh : bh;
+      const int te = r0 + tile.nr < g.m_rows ? r0 + tile.nr : g.m_rows;   // rows this tile stores
       const int co_row = mi * kBM + q * 32 + lane;
       const uint32_t tl = tmem + ab * kTNRows + (static_cast<uint32_t>(q * 32) << 16);
       if constexpr (MODE == EPI_ROWS || MODE == EPI_ROWS_CONVT) {
@@ -1274,15 +1310,15 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         }
         const bool colok = col < e.nstore;
         const float bias = (e.bias && colok) ? __ldg(e.bias + co_row) : 0.0f;
-        const int rb = ti * kTNRows + half * 128;   // this warp's first time row
-        // output row map and masks of the four blocks (lane = row within the block)
+        const int rb = r0 + 32 * b0;   // this warp's first time row
+        // output row map and masks of its (up to four) blocks (lane = row within the block)
         int orow[4];
         unsigned mk = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int tr = rb + 32 * j + lane;
           orow[j] = -1;
-          if (tr < g.m_rows) {
+          if (j < nb && tr < te) {
             if constexpr (MODE == EPI_ROWS) {
               orow[j] = tr;
             } else {
@@ -1295,12 +1331,12 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         for (int j = 0; j < 4; ++j)
           if (orow[j] >= 0) mk |= static_cast<unsigned>(__ldg(e.mask + orow[j])) << (8 * j);
         float rsA[16], acA[16];
-        tn_rows_load<MODE, F>(e, rb, col, colok, g.m_rows, rsA, acA);
+        if (nb > 0) tn_rows_load<MODE, F>(e, rb, col, colok, g.m_rows, rsA, acA);
         if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
         tc_fence_after();
-        const uint32_t tw = tl + static_cast<uint32_t>(half * 128);
+        const uint32_t tw = tl + static_cast<uint32_t>(32 * b0);
 #pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < nb; ++j) {
           const int th = rb + 32 * j;
           const unsigned mj = (mk >> (8 * j)) & 0xffu;
           const int oj = j == 0 ? orow[0] : j == 1 ? orow[1] : j == 2 ? orow[2] : orow[3];
@@ -1308,7 +1344,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
           tn_rows_load<MODE, F>(e, th + 16, col, colok, g.m_rows, rsB, acB);
           tn_rows_pass<MODE, F>(e, tw + 32u * j, th, 0, col, colok, bias, mj, oj, rsA, acA, &tmO0,
                                 &tmO1, stg, slot, lane);
-          if (j < 3) tn_rows_load<MODE, F>(e, th + 32, col, colok, g.m_rows, rsA, acA);
+          if (j + 1 < nb) tn_rows_load<MODE, F>(e, th + 32, col, colok, g.m_rows, rsA, acA);
           tn_rows_pass<MODE, F>(e, tw + 32u * j + 16u, th + 16, 1, col, colok, bias, mj, oj, rsB,
                                 acB, &tmO0, &tmO1, stg, slot, lane);
         }
@@ -1316,8 +1352,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int j = half * 4; j < half * 4 + 4; ++j)
-          tn_epi<MODE, F>(e, tl + 32u * j, z, co_row, ti * kTNRows + 32 * j, g.m_rows);
+        for (int j = b0; j < b0 + nb; ++j)
+          tn_epi<MODE, F>(e, tl + 32u * j, z, co_row, r0 + 32 * j, te);
       }
       tc_fence_before();
       __syncwarp();

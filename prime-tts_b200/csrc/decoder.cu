@@ -19,44 +19,14 @@
 //   stage; the last stage of the last resblock also does /dec/Add, /dec/Add_1, /3, LeakyRelu) ->
 //   ups.1 -> the same MRF at 128 channels (final LeakyRelu 0.01 and the (1,0) reflection pad row)
 //   -> subband_conv_post -> the iSTFT/PQMF tail kernel.
-#include <climits>
-#include <cstring>
-#include <mutex>
-#include <vector>
-
-#include "../../include/pt_b200.h"
-#include "common.cuh"
-
-namespace ptb {
-int tail_prepare();
-int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
-                  const long long *wav0, const long long *klo, const long long *khi, int nreq,
-                  long long max_tp, const float *pqmf_dev, float *wav_dev, cudaStream_t st);
-}  // namespace ptb
+#include "decoder.cuh"
 
 using namespace ptb;
+using namespace ptb::dec;
 
 namespace {
 
-constexpr int64_t kGap[3] = {8, 28, 32};
-// rows before the first request; level 2 starts every request at a row = 4 (mod 16) (a lead of
-// 36, gaps of 32, request lengths 16T), so a request's reflection row (-1) and its source (+1)
-// fall in the same 16-row epilogue pass
-constexpr int64_t kLead[3] = {8, 28, 36};
-// receptive radius of one output sample, in latent frames before / after its own frame
-// (PQMF 63 taps, overlap-add, conv_post k7, two MRF blocks reaching 60 rows, two k16/s4 convT,
-// conv_pre k7, propagated back to the latent)
-constexpr int64_t kReachLeft = 25, kReachRight = 24;
 constexpr int64_t kStreamBatchFrames = 65536;   // default latent frames per streaming batch
-constexpr int kK[3] = {3, 7, 11};
-constexpr int kD[3] = {1, 3, 5};
-constexpr float kLr = 0.10000000149011612f;
-constexpr float kLrFinal = 0.009999999776482582f;
-
-struct DLayer {
-  float *w = nullptr, *b = nullptr;  // [n_pad][ntap][cin32] tf32, bias [round_up(n_pad, 32)]
-  int n_pad = 0, bn = 0, cin32 = 0, ntap = 0;
-};
 
 // Stage packed weights into the kernel layout on the device (once per decoder).
 int make_layer(DLayer *L, const float *wp, const float *bias, int rows4, int ntap, int cin,
@@ -80,15 +50,18 @@ int make_layer(DLayer *L, const float *wp, const float *bias, int rows4, int nta
   return 0;
 }
 
-// scatter each request's channel-major latent columns (z[zoff + c*zld + t], t < T) into the
+}  // namespace
+
+// scatter each request's channel-major latent columns (z[zoff + c*zld + t], f0 <= t < T) into the
 // level-0 rows, tf32-rounded
-__global__ void stage_z_kernel(const float *__restrict__ z, const long long *__restrict__ zoff,
+__global__ void ptb::dec::stage_z_kernel(const float *__restrict__ z, const long long *__restrict__ zoff,
                                const long long *__restrict__ zld, const long long *__restrict__ T,
-                               const long long *__restrict__ a0, float *__restrict__ Z) {
+                               const long long *__restrict__ a0, const long long *__restrict__ f0,
+                               float *__restrict__ Z) {
   __shared__ float tile[32][33];
   const int r = blockIdx.z;
-  const long long Tr = T[r];
-  const long long t0 = (long long)blockIdx.x * 32;
+  const long long Tr = T[r];   // frames [f0, T) of request r (f0 null: from 0)
+  const long long t0 = (f0 ? f0[r] : 0) + (long long)blockIdx.x * 32;
   if (t0 >= Tr) return;
   const int c0 = blockIdx.y * 32;
   const float *zr = z + zoff[r];
@@ -103,65 +76,6 @@ __global__ void stage_z_kernel(const float *__restrict__ z, const long long *__r
     if (t < Tr) Z[(a0[r] + t) * 192 + c0 + threadIdx.x] = tf32_rna(tile[threadIdx.x][i]);
   }
 }
-
-struct Plan {
-  std::vector<pt_b200_window> W;   // the requests this plan lays out
-  std::vector<int64_t> T;
-  int64_t R[3] = {0, 0, 0};
-  int64_t max_T = 0, total_z = 0, total_wav = 0;
-  // device tables
-  unsigned char *mask[3] = {nullptr, nullptr, nullptr};
-  unsigned char *mask_refl = nullptr, *mask_post = nullptr;
-  int *ob01 = nullptr, *ob12 = nullptr;
-  long long *zoff = nullptr, *zld = nullptr, *Td = nullptr, *a0 = nullptr;
-  long long *row0 = nullptr, *tp = nullptr, *wav0 = nullptr, *klo = nullptr, *khi = nullptr;
-  void *table_block = nullptr;
-  size_t table_bytes = 0;
-};
-
-}  // namespace
-
-struct pt_b200_decoder {
-  int device = 0;
-  cudaStream_t stream = nullptr;
-  uint32_t *gerr = nullptr, *gerr_host = nullptr;
-  DLayer pre, ups[2], rb1[6][3], rb2[6][3], post;
-  float *pqmf = nullptr;
-  std::mutex mu;
-  Plan plan;
-  bool have_plan = false;
-  cudaEvent_t done = nullptr;   // recorded after every decode: plan changes wait for it
-  uint64_t plan_id = 0;         // bumped whenever the plan (tables, buffers) changes
-  // CUDA graph of the whole decode: captured on the second identical call (same plan, latents,
-  // output and stream), replayed after that; PT_B200_GRAPH=0 keeps every decode eager
-  int graph_on = -1;
-  cudaGraphExec_t gexec = nullptr;
-  long g_kernels = 0;           // kernels per replay (for pt_b200_kernel_launches)
-  struct GKey {
-    uint64_t plan = ~0ull;
-    const void *z = nullptr;
-    void *wav = nullptr;
-    cudaStream_t st = nullptr;
-    bool prof = false;
-    bool operator==(const GKey &o) const {
-      return plan == o.plan && z == o.z && wav == o.wav && st == o.st && prof == o.prof;
-    }
-  } g_key, g_seen;
-  // activation buffers (grown on demand, zeroed when the plan changes)
-  void *act = nullptr;
-  size_t act_bytes = 0;
-  float *Z = nullptr, *X0 = nullptr;
-  float *U[2], *LU[2], *XB[2], *XT[2], *H[2], *ACC[2], *OUT1 = nullptr, *P = nullptr, *POST = nullptr;
-  float *zbuf = nullptr, *wavbuf = nullptr;  // staging for the host-buffer entry point
-  size_t zbuf_bytes = 0, wavbuf_bytes = 0;
-  // live per-launch timing (pt_b200_decoder_profile): one event before each launch, one at the end
-  static constexpr int kMaxRec = 64;
-  bool prof = false;
-  cudaEvent_t ev[kMaxRec + 1] = {};
-  int nrec = 0;
-  int rkind[kMaxRec] = {};
-  double rflops[kMaxRec] = {}, rbytes[kMaxRec] = {};
-};
 
 namespace {
 
@@ -188,31 +102,16 @@ int check_windows(int n, const pt_b200_window *w) {
   return 0;
 }
 
-// Lay the requests out (masks, convT row maps, per-request tables) unless the previous plan had
-// the same requests.  A new plan first waits for the last decode that used the old one (any
-// stream), then uploads and zeroes on `st`, so later work on `st` is ordered after it.
-int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_window *w) {
-  Plan &p = d->plan;
-  if (d->have_plan && same_windows(p.W, nreq, w)) return 0;
+}  // namespace
+
+int ptb::dec::build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_window *w) {
   if (check_windows(nreq, w)) return -1;
-  if (d->done) PTB_CUDA(cudaEventSynchronize(d->done));
-  if (p.table_block) cudaFree(p.table_block);
-  d->have_plan = false;
-  p = Plan();
-  ++d->plan_id;
   p.W.assign(w, w + nreq);
   for (int i = 0; i < nreq; ++i) p.T.push_back(w[i].frames);
   const int64_t *T = p.T.data();
   const int64_t scale[3] = {1, 4, 16};
-  std::vector<int64_t> a[3];
-  for (int l = 0; l < 3; ++l) {
-    int64_t off = kLead[l];
-    for (int i = 0; i < nreq; ++i) {
-      a[l].push_back(off);
-      off += scale[l] * T[i] + kGap[l];
-    }
-    p.R[l] = off;
-  }
+  std::vector<int64_t> *a = p.a;
+  layout_rows(T, nreq, a, p.R);
   for (int i = 0; i < nreq; ++i)
     PTB_REQUIRE(a[2][i] % 16 == 4, "pt_b200: level-2 layout broke the reflection-row alignment");
   for (int i = 0; i < nreq; ++i) {
@@ -303,6 +202,24 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
   p.klo = tb + 7 * nreq;
   p.khi = tb + 8 * nreq;
   p.table_bytes = tot;
+  return 0;
+}
+
+namespace {
+
+// Lay the requests out (masks, convT row maps, per-request tables) unless the previous plan had
+// the same requests.  A new plan first waits for the last decode that used the old one (any
+// stream), then uploads and zeroes on `st`, so later work on `st` is ordered after it.
+int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_window *w) {
+  Plan &p = d->plan;
+  if (d->have_plan && same_windows(p.W, nreq, w)) return 0;
+  if (check_windows(nreq, w)) return -1;
+  if (d->done) PTB_CUDA(cudaEventSynchronize(d->done));
+  if (p.table_block) cudaFree(p.table_block);
+  d->have_plan = false;
+  p = Plan();
+  ++d->plan_id;
+  if (build_layout(p, st, nreq, w)) return -1;
 
   // activation buffers: grow if needed, then zero (gap rows must read as zeros)
   const size_t r0 = (size_t)p.R[0], r1 = (size_t)p.R[1], r2 = (size_t)p.R[2];
@@ -336,9 +253,11 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
   return 0;
 }
 
-// one conv layer over the ragged rows of a level
-int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act, int64_t rows,
-             int row_off0, int row_step, const EpiParams &e) {
+}  // namespace
+
+int ptb::dec::run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act,
+                       int64_t rows, int row_off0, int row_step, const EpiParams &e,
+                       const int2 *tiles, int ntiles) {
   ConvLaunch c{};
   c.act = act;
   c.act_rows = rows;
@@ -352,10 +271,25 @@ int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *
   c.g.row_off0 = row_off0;
   c.g.row_step = row_step;
   c.g.nkb = L.ntap * (L.cin32 / kBK);
+  c.g.tiles = tiles;
+  c.g.ntiles = ntiles;
   c.e = e;
   c.e.bias = L.b;
   return launch_conv(c, d->gerr, st);
 }
+
+EpiParams ptb::dec::rows_epi(const unsigned char *mask, int ldc) {
+  EpiParams e{};
+  e.mode = EPI_ROWS;
+  e.mask = mask;
+  e.nstore = ldc;
+  e.ldc = ldc;
+  e.ldc1 = ldc;
+  e.alpha1 = kLr;
+  return e;
+}
+
+namespace {
 
 // launch kinds reported by pt_b200_decoder_launch_times
 enum { LK_STAGE = 0, LK_CONV = 1, LK_CONVT = 2, LK_POST = 3, LK_TAIL = 4 };
@@ -370,17 +304,6 @@ void rec(pt_b200_decoder *d, cudaStream_t st, int kind, double flops, double byt
   ++d->nrec;
 }
 
-EpiParams rows_epi(const unsigned char *mask, int ldc) {
-  EpiParams e{};
-  e.mode = EPI_ROWS;
-  e.mask = mask;
-  e.nstore = ldc;
-  e.ldc = ldc;
-  e.ldc1 = ldc;
-  e.alpha1 = kLr;
-  return e;
-}
-
 int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *wav_dev) {
   const Plan &p = d->plan;
   const int nreq = (int)p.T.size();
@@ -393,7 +316,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
     dim3 grid((unsigned)((p.max_T + 31) / 32), 192 / 32, (unsigned)nreq);
-    stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.zld, p.Td, p.a0, d->Z);
+    stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.zld, p.Td, p.a0, nullptr, d->Z);
     PTB_CUDA(cudaGetLastError());
     count_launch();
   }
@@ -475,8 +398,8 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   }
   // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
   rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);
-  if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, p.klo, p.khi, nreq, 16 * p.max_T + 1,
-                    d->pqmf, wav_dev, st))
+  if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, p.klo, p.khi, nullptr, 0, nreq,
+                    16 * p.max_T + 1, d->pqmf, wav_dev, st))
     return -1;
   if (d->prof) cudaEventRecord(d->ev[d->nrec], st);
   return 0;

@@ -45,6 +45,7 @@ struct TailArgs {
   const long long *tp;    // per request frame count (nullptr: tp1)
   const long long *wav0;  // per request output offset (nullptr: 0): sample j goes to wav[wav0 + j]
   const long long *klo, *khi;   // per request kept samples [klo, khi) (nullptr: all)
+  const long long *jbase;       // per request first sample of CTA 0 (nullptr: 0; a multiple of kTailW)
   long long tp1;
   const float *pqmf;      // [4][63]
   float *wav;
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   const int req = blockIdx.y;
   const long long Tp = a.tp ? a.tp[req] : a.tp1;
   const long long nwav = 16 * (Tp - 1);
-  const long long j0 = (long long)blockIdx.x * kTailW;
+  const long long j0 = (a.jbase ? a.jbase[req] : 0) + (long long)blockIdx.x * kTailW;
   const long long keep_lo = a.klo ? a.klo[req] : 0, keep_hi = a.khi ? a.khi[req] : nwav;
   if (Tp < 2 || j0 >= nwav || j0 >= keep_hi || j0 + kTailW <= keep_lo) return;
   const long long Ls = 4 * (Tp - 1);
@@ -295,10 +296,12 @@ int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wa
 }
 
 // batched requests, channels-last post rows (ld = row stride); per-request tables on the device,
-// each request writing only its kept samples
+// each request writing only its kept samples.  `chunks` CTAs of kTailW samples per request start
+// at sample jbase[r] (all of a request's samples from 0 when jbase is null and chunks is 0).
 int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
-                  const long long *wav0, const long long *klo, const long long *khi, int nreq,
-                  long long max_tp, const float *pqmf_dev, float *wav_dev, cudaStream_t st) {
+                  const long long *wav0, const long long *klo, const long long *khi,
+                  const long long *jbase, long long chunks, int nreq, long long max_tp,
+                  const float *pqmf_dev, float *wav_dev, cudaStream_t st) {
   if (tail_ready()) return -1;
   TailArgs a{};
   a.post = post_dev;
@@ -309,10 +312,12 @@ int tail_run_rows(const float *post_dev, long long ld, const long long *row0, co
   a.wav0 = wav0;
   a.klo = klo;
   a.khi = khi;
+  a.jbase = jbase;
   a.pqmf = pqmf_dev;
   a.wav = wav_dev;
   const long long nwav = 16 * (max_tp - 1);
-  dim3 grid((unsigned)((nwav + kTailW - 1) / kTailW), (unsigned)nreq);
+  if (chunks <= 0) chunks = (nwav + kTailW - 1) / kTailW;
+  dim3 grid((unsigned)chunks, (unsigned)nreq);
   tail_kernel<<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
   PTB_CUDA(cudaGetLastError());
   count_launch();

@@ -132,6 +132,14 @@ _SIGS = {
                              _i64], _i64),
     "pt_b200_stream_decode": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p, C.c_int,
                                C.c_int, C.c_int, _i64, C.c_void_p], C.c_int),
+    "pt_b200_carry_open": ([C.c_void_p, C.c_int, _i64p, C.c_int], C.c_void_p),
+    "pt_b200_carry_passes": ([C.c_void_p], C.c_int),
+    "pt_b200_carry_run": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+    "pt_b200_carry_reset": ([C.c_void_p], C.c_int),
+    "pt_b200_carry_close": ([C.c_void_p], None),
+    "pt_b200_stream_decode_carry": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p, C.c_int,
+                                     C.c_void_p], C.c_int),
+    "pt_b200_carry_plan": ([C.c_int, _i64p, C.c_int, _i64p, _i64p, _i64], _i64),
     "pt_b200_decoder_profile": ([C.c_void_p, C.c_int], C.c_int),
     "pt_b200_decoder_launch_times": ([C.c_void_p, C.c_int, C.POINTER(C.c_double),
                                       C.POINTER(C.c_double), C.POINTER(C.c_double),
@@ -468,6 +476,53 @@ def stream_plan(T, win: int = STREAM_WIN, ctx: int = STREAM_CTX, exact: bool = F
                     np.int64).reshape(-1, 6)
 
 
+def carry_plan(T, chunk: int = STREAM_WIN - 2 * STREAM_CTX):
+    """The carried-state pass plan (pt_b200_carry_plan, no GPU): (passes, lo, hi), lo / hi of
+    shape [passes][streams] -- the samples [lo, hi) of each stream that each pass emits."""
+    T = np.ascontiguousarray(T, np.int64)
+    n = lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(_i64p), chunk, None, None, 0)
+    if n < 0:
+        _check(-1, "pt_b200_carry_plan")
+    lo = np.zeros((n, len(T)), np.int64)
+    hi = np.zeros((n, len(T)), np.int64)
+    lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(_i64p), chunk, lo.ctypes.data_as(_i64p),
+                             hi.ctypes.data_as(_i64p), lo.size)
+    return int(n), lo, hi
+
+
+class CarrySession:
+    """A carried-state streaming session (pt_b200_carry_*): pass k feeds latent frames
+    [k*chunk, (k+1)*chunk) of every stream and emits the samples whose inputs are complete."""
+
+    def __init__(self, decoder: "Decoder", T, chunk: int = STREAM_WIN - 2 * STREAM_CTX):
+        self.T = np.ascontiguousarray(T, np.int64)
+        self.h = lib().pt_b200_carry_open(decoder.h, len(self.T), self.T.ctypes.data_as(_i64p),
+                                          chunk)
+        if not self.h:
+            _check(-1, "pt_b200_carry_open")
+        self.passes = lib().pt_b200_carry_passes(self.h)
+
+    def run(self, k: int, z_dev: int, wav_dev: int, stream=None) -> None:
+        _check(lib().pt_b200_carry_run(self.h, stream, k, z_dev, wav_dev), "pt_b200_carry_run")
+
+    def run_all(self, z_dev: int, wav_dev: int, stream=None) -> None:
+        """Rewind, then every pass (asynchronous on `stream`)."""
+        _check(lib().pt_b200_carry_reset(self.h), "pt_b200_carry_reset")
+        for k in range(self.passes):
+            self.run(k, z_dev, wav_dev, stream)
+
+    def close(self) -> None:
+        if self.h:
+            lib().pt_b200_carry_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def decoder_gflop(T: int) -> float:
     """Algorithmic GFLOP of one decoder request of T frames (2 x MACs; convT counted without the
     zero-stuffed MACs; the tail's einsum / OLA / PQMF included)."""
@@ -581,6 +636,32 @@ class Decoder:
         self.stream_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), win, ctx, exact, max_frames,
                            s.cuda_stream)
         self.sync(s.cuda_stream)
+        wav = wav_dev.cpu().numpy()
+        out, o = [], 0
+        for t in T:
+            out.append(wav[o:o + 256 * int(t)])
+            o += 256 * int(t)
+        return out
+
+    def stream_carry_device(self, T, z_dev: int, wav_dev: int,
+                            chunk: int = STREAM_WIN - 2 * STREAM_CTX, stream=None) -> None:
+        """Carried-state streaming of every stream (device buffers laid out as for
+        stream_device): open a session, run its passes, close it; synchronous."""
+        T = np.ascontiguousarray(T, np.int64)
+        _check(lib().pt_b200_stream_decode_carry(self.h, stream, len(T), T.ctypes.data_as(_i64p),
+                                                 z_dev, chunk, wav_dev),
+               "pt_b200_stream_decode_carry")
+
+    def stream_carry(self, zs: list, chunk: int = STREAM_WIN - 2 * STREAM_CTX) -> list:
+        """Host in, host out: each stream's z [192][T_i] -> its wav [256*T_i], carried state."""
+        import torch
+        T = np.array([z.shape[-1] for z in zs], np.int64)
+        zcat = np.concatenate([np.ascontiguousarray(z, np.float32).ravel() for z in zs])
+        dev = torch.device("cuda", self.device)
+        z_dev = torch.from_numpy(zcat).to(dev)
+        wav_dev = torch.full((int(256 * T.sum()),), float("nan"), device=dev)
+        s = torch.cuda.Stream(device=dev)
+        self.stream_carry_device(T, z_dev.data_ptr(), wav_dev.data_ptr(), chunk, s.cuda_stream)
         wav = wav_dev.cpu().numpy()
         out, o = [], 0
         for t in T:

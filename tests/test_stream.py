@@ -94,3 +94,50 @@ def test_reference_scheme_deviation_on_the_reference_cpu(weights, ref_available)
           f"max|d| {m['max_abs']:.3e}  SNDR {m['sndr_db']:.1f} dB")
     assert got.shape == full.shape
     assert m["max_abs"] > 1e-6 and m["sndr_db"] > 20.0
+
+
+# ---- carried-state streaming: the pass plan (pt_b200_carry_plan) -----------------------------
+
+CARRY_CHUNKS = [1, 7, 32, 64, 1000]
+
+
+@pytest.mark.parametrize("chunk", CARRY_CHUNKS)
+def test_carry_plan_emits_every_sample_once_in_order(chunk):
+    """Pass after pass, each stream's emitted ranges are contiguous, start at 0, never go back,
+    and the stream's last pass (the one that delivers its last frame) ends at 256 T."""
+    n, lo, hi = pt_b200.carry_plan(CASES_T, chunk)
+    assert n == -(-max(CASES_T) // chunk)
+    for s, T in enumerate(CASES_T):
+        assert lo[0, s] == 0
+        np.testing.assert_array_equal(lo[1:, s], hi[:-1, s])
+        assert (hi[:, s] >= lo[:, s]).all()
+        last = -(-T // chunk) - 1
+        assert hi[last, s] == 256 * T and (hi[last:, s] == 256 * T).all()
+
+
+@pytest.mark.parametrize("chunk", CARRY_CHUNKS)
+def test_carry_plan_emits_only_samples_whose_frames_have_arrived(chunk):
+    """A sample of latent frame f needs frames up to f + 24 (the receptive radius): before a
+    stream's last frame has arrived, a pass may emit only samples of frames <= arrived - 25."""
+    n, lo, hi = pt_b200.carry_plan(CASES_T, chunk)
+    for s, T in enumerate(CASES_T):
+        for k in range(n):
+            arrived = min(T, (k + 1) * chunk)
+            if arrived < T and hi[k, s] > 0:
+                assert (hi[k, s] - 1) // 256 <= arrived - 25, (T, chunk, k)
+
+
+def test_carry_plan_delay_at_the_reference_chunk():
+    """At 32 new frames per pass (the reference's 64-frame windows with 16 frames of context),
+    a long stream's emission trails its arrived frames by at least the 24-frame look-ahead and
+    at most 40 frames (the 16-row rounding of the level-1 resblock convs adds the rest)."""
+    n, lo, hi = pt_b200.carry_plan([1000], 32)
+    lag = [min(1000, 32 * (k + 1)) - hi[k, 0] / 256 for k in range(n - 1)]
+    assert min(lag) >= 24.0 and max(lag) <= 40.0, lag
+
+
+def test_carry_plan_rejects_bad_arguments():
+    for T, chunk in (([1, 50], 32), ([50], 0), ([], 32)):
+        Ta = np.ascontiguousarray(T, np.int64)
+        assert pt_b200.lib().pt_b200_carry_plan(len(Ta), Ta.ctypes.data_as(pt_b200._i64p), chunk,
+                                                None, None, 0) == -1

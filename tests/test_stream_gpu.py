@@ -101,3 +101,76 @@ def test_config5_streams(dec):
           f"whole decode: max|d| {float(d.max()):.3e}, worst-stream SNDR {worst_sndr:.1f} dB; "
           f"exact scheme: bitwise equal")
     assert torch.isfinite(refs).all() and worst_sndr > 20.0
+
+
+# ---- carried-state streaming (pt_b200_carry_*) ------------------------------------------------
+
+@pytest.mark.parametrize("chunk", [32, 7, 64, 1000])
+def test_carried_stream_equals_whole_decode(dec, chunk):
+    """Chunk by chunk with carried state, every row computed once: the whole decode's bits."""
+    zs = _zs(EDGE_T, 24)
+    full = dec.decode(zs)
+    got = dec.stream_carry(zs, chunk)
+    for T, a, b in zip(EDGE_T, got, full):
+        np.testing.assert_array_equal(a, b, err_msg=f"T={T} chunk={chunk}")
+
+
+def test_carried_passes_read_only_arrived_frames(dec):
+    """Pass by pass with the latents still to come set to NaN: each pass reads only frames that
+    have arrived (a NaN would reach the output) and writes only the samples it emits (the rest of
+    the waveform stays NaN until its pass), and every emitted sample is final."""
+    import torch
+    Ts, chunk = [2, 40, 97, 300, 65], 32
+    zs = _zs(Ts, 25)
+    full = np.concatenate(dec.decode(zs))
+    dev = torch.device("cuda", 0)
+    zreal = [torch.from_numpy(z).to(dev) for z in zs]
+    z = torch.full((192 * sum(Ts),), float("nan"), device=dev)
+    wav = torch.full((256 * sum(Ts),), float("nan"), device=dev)
+    s = torch.cuda.Stream(device=dev)
+    n, lo, hi = pt_b200.carry_plan(Ts, chunk)
+    sess = pt_b200.CarrySession(dec, Ts, chunk)
+    try:
+        assert sess.passes == n
+        for k in range(n):
+            zo = 0
+            for T, zr in zip(Ts, zreal):   # frames [k*chunk, (k+1)*chunk) arrive
+                a, b = min(T, k * chunk), min(T, (k + 1) * chunk)
+                z[zo:zo + 192 * T].view(192, T)[:, a:b] = zr[:, a:b]
+                zo += 192 * T
+            torch.cuda.synchronize()
+            sess.run(k, z.data_ptr(), wav.data_ptr(), s.cuda_stream)
+            dec.sync(s.cuda_stream)
+            w = wav.cpu().numpy()
+            wo = 0
+            for i, T in enumerate(Ts):
+                np.testing.assert_array_equal(w[wo:wo + hi[k, i]], full[wo:wo + hi[k, i]])
+                assert np.isnan(w[wo + hi[k, i]:wo + 256 * T]).all(), (k, T)
+                wo += 256 * T
+    finally:
+        sess.close()
+    with pytest.raises(pt_b200.PtB200Error):   # passes run in order, each once
+        bad = pt_b200.CarrySession(dec, Ts, chunk)
+        try:
+            bad.run(1, z.data_ptr(), wav.data_ptr(), s.cuda_stream)
+        finally:
+            bad.close()
+
+
+def test_config5_carried(dec):
+    """Config 5 at full size (512 streams, seed 4) with carried state, 32 new frames per pass
+    (the reference's 64-frame windows with 16 frames of context): the whole decode's bits, with
+    no frame decoded twice."""
+    import torch
+    T, zs = pt_b200.config5()
+    Ta = np.array(T, np.int64)
+    dev = torch.device("cuda", 0)
+    z = torch.from_numpy(np.concatenate([a.ravel() for a in zs])).to(dev)
+    n = int(256 * Ta.sum())
+    full = torch.empty(n, device=dev)
+    got = torch.full((n,), float("nan"), device=dev)
+    s = torch.cuda.Stream(device=dev)
+    dec.decode_device(Ta, z.data_ptr(), full.data_ptr(), s.cuda_stream)
+    dec.sync(s.cuda_stream)
+    dec.stream_carry_device(Ta, z.data_ptr(), got.data_ptr(), 32, s.cuda_stream)
+    assert torch.equal(got, full)
