@@ -48,6 +48,9 @@ struct ConvGeom {
   // executor computes only each stream's newly computable rows of a layer.
   const int2 *tiles;
   int ntiles;
+  // Channels-on-M kernel only: walk the tiles last to first, so that a layer starts on the rows
+  // its producer wrote last (still in L2); the decoder alternates it between layers.
+  int reverse;
 };
 
 struct EpiParams {
@@ -908,8 +911,9 @@ struct TNCfg {
 struct TNTile {
   int z, mi, r0, nr;
 };
-__device__ __forceinline__ TNTile tn_tile(const ConvGeom &g, int t, int mt, int tt) {
+__device__ __forceinline__ TNTile tn_tile(const ConvGeom &g, int t, int mt, int tt, int ntiles) {
   TNTile x;
+  if (g.reverse) t = ntiles - 1 - t;
   if (g.tiles) {
     const int entry = t / mt;
     const int2 v = g.tiles[entry];
@@ -1194,7 +1198,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       bool ok = true;
       int cw = 0, ca = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TNTile tl = tn_tile(g, t, mt, tt);
+        const TNTile tl = tn_tile(g, t, mt, tt, ntiles);
         const int z = tl.z, mi = tl.mi;
         const int wlo = tl.r0 + g.row_off0 + lo_off;
         const int nbox = (tl.nr + wspan + kWinBox - 1) / kWinBox;
@@ -1244,7 +1248,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       bool ok = true;
       int cw = 0, ca = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-        const uint32_t idesc = idesc_tf32(kBM, tn_tile(g, t, mt, tt).nr);
+        const uint32_t idesc = idesc_tf32(kBM, tn_tile(g, t, mt, tt, ntiles).nr);
         const int ab = it & 1;
         if (!mbar_wait(aempty(ab), ((it >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
           ok = false;
@@ -1294,7 +1298,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int ab = it & 1;
-      const TNTile tile = tn_tile(g, t, mt, tt);
+      const TNTile tile = tn_tile(g, t, mt, tt, ntiles);
       const int z = tile.z, mi = tile.mi, r0 = tile.r0;
       // this warp's 32-row blocks of the tile: half 0 takes the first ceil(nblk / 2)
       const int nblk = (tile.nr + 31) / 32, bh = (nblk + 1) / 2;

@@ -257,7 +257,7 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
 
 int ptb::dec::run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act,
                        int64_t rows, int row_off0, int row_step, const EpiParams &e,
-                       const int2 *tiles, int ntiles) {
+                       const int2 *tiles, int ntiles, int reverse) {
   ConvLaunch c{};
   c.act = act;
   c.act_rows = rows;
@@ -273,6 +273,7 @@ int ptb::dec::run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, con
   c.g.nkb = L.ntap * (L.cin32 / kBK);
   c.g.tiles = tiles;
   c.g.ntiles = ntiles;
+  c.g.reverse = reverse;
   c.e = e;
   c.e.bias = L.b;
   return launch_conv(c, d->gerr, st);
@@ -312,6 +313,12 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   for (int64_t t : p.T) frames += (double)t;
   // algorithmic work of one conv layer over every request's valid rows (2 x MACs)
   auto cflops = [&](double rows, int cin, int cout, int K) { return 2.0 * rows * cin * cout * K; };
+  // every other conv launch walks its tiles last to first, starting on the rows its producer
+  // wrote last, which are still in L2 (PT_B200_ALT=0: all forward)
+  static int alt = -1;
+  if (alt < 0) alt = getenv("PT_B200_ALT") ? atoi(getenv("PT_B200_ALT")) : 1;
+  int nconv = 0;
+  auto rev = [&]() { return alt ? (nconv++ & 1) : 0; };
   // latents -> level-0 rows
   rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
@@ -325,7 +332,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   {
     EpiParams e = rows_epi(p.mask[0], 512);
     e.out1 = d->X0;
-    if (run_conv(d, st, d->pre, d->Z, p.R[0], -3, 1, e)) return -1;
+    if (run_conv(d, st, d->pre, d->Z, p.R[0], -3, 1, e, nullptr, 0, rev())) return -1;
   }
   const float *lvl_in = d->X0;
   for (int s = 0; s < 2; ++s) {
@@ -343,7 +350,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
       e.cphase = C;
       e.out0 = d->U[s];
       e.out1 = d->LU[s];
-      if (run_conv(d, st, d->ups[s], lvl_in, rin, 0, -1, e)) return -1;
+      if (run_conv(d, st, d->ups[s], lvl_in, rin, 0, -1, e, nullptr, 0, rev())) return -1;
     }
     for (int rb = 0; rb < 3; ++rb) {
       const int r = 3 * s + rb, K = kK[rb];
@@ -353,7 +360,9 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
           EpiParams e = rows_epi(mk, C);
           e.out1 = d->H[s];
           const float *in = j == 0 ? d->LU[s] : d->XT[s];
-          if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e)) return -1;
+          if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e, nullptr, 0,
+                       rev()))
+            return -1;
         }
         // convs2 bytes: input + residual + outputs (+ the branch sum read by resblocks 1, 2)
         const int nio = j < 2 ? 4 : rb == 0 ? 3 : 4;
@@ -382,7 +391,8 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
               e.refl = 1;
             }
           }
-          if (run_conv(d, st, d->rb2[r][j], d->H[s], rout, -(K - 1) / 2, 1, e)) return -1;
+          if (run_conv(d, st, d->rb2[r][j], d->H[s], rout, -(K - 1) / 2, 1, e, nullptr, 0, rev()))
+            return -1;
         }
       }
     }
@@ -394,7 +404,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   {
     EpiParams e = rows_epi(p.mask_post, 80);
     e.out0 = d->POST;
-    if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e)) return -1;
+    if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e, nullptr, 0, rev())) return -1;
   }
   // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
   rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);

@@ -80,7 +80,7 @@ int build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_window *w);
 // one conv layer over the rows of a level (all of them, or the tile list {first row, rows})
 int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act, int64_t rows,
              int row_off0, int row_step, const EpiParams &e, const int2 *tiles = nullptr,
-             int ntiles = 0);
+             int ntiles = 0, int reverse = 0);
 EpiParams rows_epi(const unsigned char *mask, int ldc);
 
 // latents -> level-0 rows: frames [f0, T) of every request (f0 null: from 0), tf32-rounded
