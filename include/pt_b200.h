@@ -239,6 +239,21 @@ PT_B200_API int pt_b200_decode_batch_device(pt_b200_decoder *d, void *stream, in
                                 const float *z_dev, float *wav_dev);
 PT_B200_API int pt_b200_decoder_sync(pt_b200_decoder *d, void *stream);
 
+/* Pipelined host-buffer decodes (a server's steady state): each call queues the upload of z_host
+ * into one of two device staging slots, the decode, and the download of the waveform into
+ * wav_host, and returns at once.  Uploads and downloads run on their own streams, so batch k+1's
+ * upload and batch k's download overlap batch k's decode (host buffers must be pinned).  A call
+ * reuses the slot of the call before the previous one only after that call's decode and download
+ * are done.  One thread at a time; the host buffers of a call must stay valid until
+ * pt_b200_decode_async_wait() returns (it waits for every queued call and reports device errors).
+ * pt_b200_decode_async_streams() hands out the upload, decode and download streams (created on
+ * first use) for callers that order their own work around the pipeline. */
+PT_B200_API int pt_b200_decode_batch_async(pt_b200_decoder *d, int nreq, const int64_t *T,
+                                           const float *z_host, float *wav_host);
+PT_B200_API int pt_b200_decode_async_wait(pt_b200_decoder *d);
+PT_B200_API int pt_b200_decode_async_streams(pt_b200_decoder *d, void **upload, void **decode,
+                                             void **download);
+
 /* Live per-launch timing of the decoder, for the benchmark's roofline: with profiling enabled
  * every decode records a CUDA event before each of its launches (and one after the last) on the
  * decode stream.  After the decode has been synchronised, pt_b200_decoder_launch_times fills, per

@@ -494,7 +494,23 @@ void pt_b200_decoder_destroy(pt_b200_decoder *d) {
   for (auto &e : d->ev)
     if (e) cudaEventDestroy(e);
   if (d->done) cudaEventDestroy(d->done);
-  if (d->gexec) cudaGraphExecDestroy(d->gexec);
+  for (auto &g : d->gexec)
+    if (g) cudaGraphExecDestroy(g);
+  if (d->h2d) {
+    cudaStreamSynchronize(d->h2d);
+    cudaStreamDestroy(d->h2d);
+  }
+  if (d->d2h) {
+    cudaStreamSynchronize(d->d2h);
+    cudaStreamDestroy(d->d2h);
+  }
+  for (int s = 0; s < 2; ++s) {
+    if (d->ev_up[s]) cudaEventDestroy(d->ev_up[s]);
+    if (d->ev_dec[s]) cudaEventDestroy(d->ev_dec[s]);
+    if (d->ev_down[s]) cudaEventDestroy(d->ev_down[s]);
+    if (d->az[s]) cudaFree(d->az[s]);
+    if (d->aw[s]) cudaFree(d->aw[s]);
+  }
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
 }
@@ -508,13 +524,22 @@ int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n, const pt_b20
   if (build_plan(d, st, n, w)) return -1;
   if (d->graph_on < 0) d->graph_on = getenv("PT_B200_GRAPH") ? atoi(getenv("PT_B200_GRAPH")) : 1;
   const pt_b200_decoder::GKey key{d->plan_id, z_dev, wav_dev, st, d->prof};
+  constexpr int NG = pt_b200_decoder::kGraphs;
+  int hit = -1;
+  bool seen = false;
+  for (int i = 0; i < NG; ++i) {
+    if (d->gexec[i] && key == d->g_key[i]) hit = i;
+    if (key == d->g_seen[i]) seen = true;
+  }
   // profiled decodes stay eager: events recorded by graph nodes cannot be timed
-  if (d->graph_on && !d->prof && (key == d->g_key || key == d->g_seen)) {
-    if (!(key == d->g_key)) {
-      // second identical call: capture the decode once, then replay it
-      if (d->gexec) cudaGraphExecDestroy(d->gexec);
-      d->gexec = nullptr;
-      d->g_key = pt_b200_decoder::GKey{};
+  if (d->graph_on && !d->prof && (hit >= 0 || seen)) {
+    if (hit < 0) {
+      // second identical call: capture the decode once (into the older slot), then replay it
+      hit = d->g_next;
+      d->g_next = (d->g_next + 1) % NG;
+      if (d->gexec[hit]) cudaGraphExecDestroy(d->gexec[hit]);
+      d->gexec[hit] = nullptr;
+      d->g_key[hit] = pt_b200_decoder::GKey{};
       if (tail_prepare()) return -1;   // one-time constant uploads happen outside the capture
       const long before = launches(0);
       PTB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
@@ -527,16 +552,17 @@ int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n, const pt_b20
         if (g) cudaGraphDestroy(g);
         PTB_REQUIRE(false, "pt_b200: decode graph capture failed (%s)", cudaGetErrorString(ec));
       }
-      const cudaError_t ei = cudaGraphInstantiate(&d->gexec, g, 0);
+      const cudaError_t ei = cudaGraphInstantiate(&d->gexec[hit], g, 0);
       cudaGraphDestroy(g);
       PTB_CUDA(ei);
-      d->g_kernels = captured;
-      d->g_key = key;
+      d->g_kernels[hit] = captured;
+      d->g_key[hit] = key;
     }
-    PTB_CUDA(cudaGraphLaunch(d->gexec, st));
-    count_launch(d->g_kernels);
+    PTB_CUDA(cudaGraphLaunch(d->gexec[hit], st));
+    count_launch(d->g_kernels[hit]);
   } else {
-    d->g_seen = key;
+    d->g_seen[d->g_seen_next] = key;
+    d->g_seen_next = (d->g_seen_next + 1) % NG;
     if (run_decoder(d, st, z_dev, wav_dev)) return -1;
   }
   PTB_CUDA(cudaEventRecord(d->done, st));
@@ -671,6 +697,93 @@ int pt_b200_decode_batch(pt_b200_decoder *d, void *stream, int nreq, const int64
   if (pt_b200_decode_batch_device(d, st, nreq, T, d->zbuf, d->wavbuf)) return -1;
   PTB_CUDA(cudaMemcpyAsync(wav_host, d->wavbuf, (size_t)nw * 4, cudaMemcpyDeviceToHost, st));
   return pt_b200_decoder_sync(d, st);
+}
+
+namespace {
+
+// the upload / download streams and the per-slot events of the pipelined entry point
+int async_setup(pt_b200_decoder *d) {
+  if (d->h2d) return 0;
+  PTB_CUDA(cudaStreamCreateWithFlags(&d->h2d, cudaStreamNonBlocking));
+  PTB_CUDA(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+  for (int s = 0; s < 2; ++s) {
+    PTB_CUDA(cudaEventCreateWithFlags(&d->ev_up[s], cudaEventDisableTiming));
+    PTB_CUDA(cudaEventCreateWithFlags(&d->ev_dec[s], cudaEventDisableTiming));
+    PTB_CUDA(cudaEventCreateWithFlags(&d->ev_down[s], cudaEventDisableTiming));
+  }
+  return 0;
+}
+
+}  // namespace
+
+int pt_b200_decode_batch_async(pt_b200_decoder *d, int nreq, const int64_t *T, const float *z_host,
+                               float *wav_host) {
+  PTB_REQUIRE(d && T && z_host && wav_host && nreq > 0, "pt_b200: bad decode arguments");
+  int64_t nz = 0, nw = 0;
+  for (int i = 0; i < nreq; ++i) {
+    nz += 192 * T[i];
+    nw += 256 * T[i];
+  }
+  int s = 0;
+  {
+    std::lock_guard<std::mutex> lk(d->mu);
+    PTB_CUDA(cudaSetDevice(d->device));
+    if (async_setup(d)) return -1;
+    if ((size_t)nz * 4 > d->az_bytes || (size_t)nw * 4 > d->aw_bytes) {
+      // grow both slots once nothing in flight uses them
+      PTB_CUDA(cudaStreamSynchronize(d->h2d));
+      PTB_CUDA(cudaStreamSynchronize(d->stream));
+      PTB_CUDA(cudaStreamSynchronize(d->d2h));
+      for (int k = 0; k < 2; ++k) {
+        if (d->az[k]) cudaFree(d->az[k]);
+        if (d->aw[k]) cudaFree(d->aw[k]);
+        d->az[k] = d->aw[k] = nullptr;
+        d->slot_used[k] = false;
+      }
+      d->az_bytes = d->aw_bytes = 0;
+      for (int k = 0; k < 2; ++k) {
+        PTB_CUDA(cudaMalloc(&d->az[k], (size_t)nz * 4));
+        PTB_CUDA(cudaMalloc(&d->aw[k], (size_t)nw * 4));
+      }
+      d->az_bytes = (size_t)nz * 4;
+      d->aw_bytes = (size_t)nw * 4;
+    }
+    s = d->async_next;
+    d->async_next ^= 1;
+    // upload into slot s once the decode that read it last has finished
+    if (d->slot_used[s]) PTB_CUDA(cudaStreamWaitEvent(d->h2d, d->ev_dec[s], 0));
+    PTB_CUDA(cudaMemcpyAsync(d->az[s], z_host, (size_t)nz * 4, cudaMemcpyHostToDevice, d->h2d));
+    PTB_CUDA(cudaEventRecord(d->ev_up[s], d->h2d));
+    // the decode waits for its upload and for the download that last read its output slot
+    PTB_CUDA(cudaStreamWaitEvent(d->stream, d->ev_up[s], 0));
+    if (d->slot_used[s]) PTB_CUDA(cudaStreamWaitEvent(d->stream, d->ev_down[s], 0));
+  }
+  if (pt_b200_decode_batch_device(d, d->stream, nreq, T, d->az[s], d->aw[s])) return -1;
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaEventRecord(d->ev_dec[s], d->stream));
+  PTB_CUDA(cudaStreamWaitEvent(d->d2h, d->ev_dec[s], 0));
+  PTB_CUDA(cudaMemcpyAsync(wav_host, d->aw[s], (size_t)nw * 4, cudaMemcpyDeviceToHost, d->d2h));
+  PTB_CUDA(cudaEventRecord(d->ev_down[s], d->d2h));
+  d->slot_used[s] = true;
+  return 0;
+}
+
+int pt_b200_decode_async_wait(pt_b200_decoder *d) {
+  PTB_REQUIRE(d, "pt_b200: NULL decoder");
+  PTB_CUDA(cudaSetDevice(d->device));
+  if (d->d2h) PTB_CUDA(cudaStreamSynchronize(d->d2h));   // downloads follow every decode
+  return pt_b200_decoder_sync(d, d->stream);
+}
+
+int pt_b200_decode_async_streams(pt_b200_decoder *d, void **upload, void **decode, void **download) {
+  PTB_REQUIRE(d, "pt_b200: NULL decoder");
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  if (async_setup(d)) return -1;
+  if (upload) *upload = d->h2d;
+  if (decode) *decode = d->stream;
+  if (download) *download = d->d2h;
+  return 0;
 }
 
 int pt_b200_decoder_profile(pt_b200_decoder *d, int enable) {

@@ -103,11 +103,14 @@ struct pt_b200_decoder {
   bool have_plan = false;
   cudaEvent_t done = nullptr;   // recorded after every decode: plan changes wait for it
   uint64_t plan_id = 0;         // bumped whenever the plan (tables, buffers) changes
-  // CUDA graph of the whole decode: captured on the second identical call (same plan, latents,
-  // output and stream), replayed after that; PT_B200_GRAPH=0 keeps every decode eager
+  // CUDA graphs of the whole decode: captured on the second identical call (same plan, latents,
+  // output and stream), replayed after that; two are kept, so the two staging slots of the
+  // pipelined host entry point both replay; PT_B200_GRAPH=0 keeps every decode eager
+  static constexpr int kGraphs = 2;
   int graph_on = -1;
-  cudaGraphExec_t gexec = nullptr;
-  long g_kernels = 0;           // kernels per replay (for pt_b200_kernel_launches)
+  cudaGraphExec_t gexec[kGraphs] = {};
+  long g_kernels[kGraphs] = {};  // kernels per replay (for pt_b200_kernel_launches)
+  int g_next = 0, g_seen_next = 0;
   struct GKey {
     uint64_t plan = ~0ull;
     const void *z = nullptr;
@@ -117,7 +120,7 @@ struct pt_b200_decoder {
     bool operator==(const GKey &o) const {
       return plan == o.plan && z == o.z && wav == o.wav && st == o.st && prof == o.prof;
     }
-  } g_key, g_seen;
+  } g_key[kGraphs], g_seen[kGraphs];
   // activation buffers (grown on demand, zeroed when the plan changes)
   void *act = nullptr;
   size_t act_bytes = 0;
@@ -125,6 +128,14 @@ struct pt_b200_decoder {
   float *U[2], *LU[2], *XB[2], *XT[2], *H[2], *ACC[2], *OUT1 = nullptr, *P = nullptr, *POST = nullptr;
   float *zbuf = nullptr, *wavbuf = nullptr;  // staging for the host-buffer entry point
   size_t zbuf_bytes = 0, wavbuf_bytes = 0;
+  // pipelined host-buffer decodes (pt_b200_decode_batch_async): two staging slots, an upload and
+  // a download stream beside the decode stream
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_up[2] = {}, ev_dec[2] = {}, ev_down[2] = {};
+  bool slot_used[2] = {false, false};
+  float *az[2] = {}, *aw[2] = {};
+  size_t az_bytes = 0, aw_bytes = 0;
+  int async_next = 0;
   // live per-launch timing (pt_b200_decoder_profile): one event before each launch, one at the end
   static constexpr int kMaxRec = 64;
   bool prof = false;

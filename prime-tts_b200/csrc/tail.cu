@@ -142,15 +142,18 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     const int fl = it >> 6, b = (it >> 4) & 3;
     const int fl2 = two ? it2 >> 6 : fl, b2 = (it2 >> 4) & 3;
     double er = 0.0, ei = 0.0, er2 = 0.0, ei2 = 0.0;
+    // zero basis entries are skipped, as in the reference einsum.  Each product of two fp32
+    // values (24-bit significands) is exact in double, so one fused multiply-add rounds exactly
+    // where the reference's multiply-then-add does (its multiply is exact): the same bits.
 #pragma unroll
-    for (int k = 0; k < 9; ++k) {   // zero basis entries are skipped, as in the reference einsum
+    for (int k = 0; k < 9; ++k) {
       if (bcn[k] != 0.0) {
-        er = __dadd_rn(er, __dmul_rn(bcn[k], re[fl][b][k]));
-        er2 = __dadd_rn(er2, __dmul_rn(bcn[k], re[fl2][b2][k]));
+        er = __fma_rn(bcn[k], re[fl][b][k], er);
+        er2 = __fma_rn(bcn[k], re[fl2][b2][k], er2);
       }
       if (bsn[k] != 0.0) {
-        ei = __dadd_rn(ei, __dmul_rn(bsn[k], im[fl][b][k]));
-        ei2 = __dadd_rn(ei2, __dmul_rn(bsn[k], im[fl2][b2][k]));
+        ei = __fma_rn(bsn[k], im[fl][b][k], ei);
+        ei2 = __fma_rn(bsn[k], im[fl2][b2][k], ei2);
       }
     }
     fr[fl][b * 16 + n] = __fmul_rn(__fadd_rn((float)er, (float)ei), wn);

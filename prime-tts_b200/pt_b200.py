@@ -126,6 +126,10 @@ _SIGS = {
     "pt_b200_decode_batch_device": ([C.c_void_p, C.c_void_p, C.c_int, _i64p, C.c_void_p,
                                      C.c_void_p], C.c_int),
     "pt_b200_decoder_sync": ([C.c_void_p, C.c_void_p], C.c_int),
+    "pt_b200_decode_batch_async": ([C.c_void_p, C.c_int, _i64p, C.c_void_p, C.c_void_p], C.c_int),
+    "pt_b200_decode_async_wait": ([C.c_void_p], C.c_int),
+    "pt_b200_decode_async_streams": ([C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                      C.POINTER(C.c_void_p)], C.c_int),
     "pt_b200_decode_windows": ([C.c_void_p, C.c_void_p, C.c_int, C.POINTER(WindowC), C.c_void_p,
                                 C.c_void_p], C.c_int),
     "pt_b200_stream_plan": ([C.c_int, _i64p, C.c_int, C.c_int, C.c_int, C.POINTER(WindowC),
@@ -599,6 +603,23 @@ class Decoder:
         """Concatenated host buffers given by address (pinned buffers in bench.py)."""
         _check(lib().pt_b200_decode_batch(self.h, stream, len(T), T.ctypes.data_as(_i64p),
                                           z_ptr, wav_ptr), "pt_b200_decode_batch")
+
+    def decode_async(self, T: np.ndarray, z_ptr: int, wav_ptr: int) -> None:
+        """Pipelined host-buffer decode (pinned buffers): queue upload, decode and download and
+        return; decode_async_wait() joins every queued call."""
+        T = np.ascontiguousarray(T, np.int64)
+        _check(lib().pt_b200_decode_batch_async(self.h, len(T), T.ctypes.data_as(_i64p), z_ptr,
+                                                wav_ptr), "pt_b200_decode_batch_async")
+
+    def decode_async_wait(self) -> None:
+        _check(lib().pt_b200_decode_async_wait(self.h), "pt_b200_decode_async_wait")
+
+    def async_streams(self):
+        """(upload, decode, download) cudaStream_t handles of the pipelined entry point."""
+        up, dec, down = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        _check(lib().pt_b200_decode_async_streams(self.h, C.byref(up), C.byref(dec),
+                                                  C.byref(down)), "pt_b200_decode_async_streams")
+        return up.value, dec.value, down.value
 
     def decode_device(self, T: np.ndarray, z_dev: int, wav_dev: int, stream=None) -> None:
         """Concatenated device buffers (addresses), asynchronous on `stream`."""

@@ -164,3 +164,24 @@ def test_decoder_from_container(tmp_path, orc):
         np.testing.assert_array_equal(wav, got)
     finally:
         pt_b200.lib().pt_b200_decoder_destroy(h)
+
+
+def test_pipelined_host_decodes_match_the_synchronous_ones(dec):
+    """pt_b200_decode_batch_async: calls queued back to back (two staging slots in turn, each
+    captured and replayed as its own graph, a bigger batch growing the slots midway) return the
+    same bits as one synchronous host decode per batch, in every output buffer."""
+    import torch
+    batches = [pt_b200.config4(seed=s, n=5, lo=20, hi=70) for s in (7, 8)]
+    batches.append(pt_b200.config4(seed=9, n=7, lo=60, hi=140))   # grows the staging slots
+    calls = [0, 1, 0, 1, 0, 2, 2, 1, 2]
+    zh, wh, refs = [], [], []
+    for T, zs in batches:
+        zh.append(torch.from_numpy(np.concatenate([a.ravel() for a in zs])).pin_memory())
+        refs.append(np.concatenate(dec.decode(zs)))
+    for b in calls:
+        w = torch.full((int(256 * sum(batches[b][0])),), float("nan")).pin_memory()
+        wh.append(w)
+        dec.decode_async(np.array(batches[b][0], np.int64), zh[b].data_ptr(), w.data_ptr())
+    dec.decode_async_wait()
+    for b, w in zip(calls, wh):
+        np.testing.assert_array_equal(w.numpy(), refs[b])
