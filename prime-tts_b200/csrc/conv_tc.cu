@@ -221,7 +221,7 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
     std::lock_guard<std::mutex> lk(mu);
     if (!((attr_done >> dev) & 1ull)) {
       PTB_CUDA(cudaFuncSetAttribute(conv_tc_tn_kernel<MODE, F>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg::kBytes));
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg<F>::kBytes));
       attr_done |= 1ull << dev;
     }
   }
@@ -246,7 +246,7 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   ConvGeom g = L.g;
   g.nbatch = L.batch;
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);
+  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg<F>::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;

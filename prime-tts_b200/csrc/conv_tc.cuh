@@ -893,14 +893,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
 constexpr int kTNRows = 256;    // time rows per tile (MMA N)
 constexpr int kTNThreads = 320; // warps 0-7 epilogue, 8 TMA producer, 9 TMEM allocator + MMA
 
+// Pipeline shape.  The convs1 instances (no residual) are tensor-bound: 2 activation-window slots
+// and 7 weight stages.  The residual-reading convs2 instances trade weight stages for a third
+// window slot, which keeps their window loads further ahead of the MMAs while the epilogue's
+// residual reads load the memory system (3-12 us a layer on config 4; the convs1 layers lose
+// 2-6 us with fewer weight stages, so they keep 7).
+template <int F>
 struct TNCfg {
+  static constexpr int kWinSlots = (F != EF_GENERIC && (F & EF_RES)) ? 3 : 2;
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
-  static constexpr int kAStages = 7;
+  static constexpr int kAStages = kWinSlots == 3 ? 4 : 7;
   static constexpr int kStageWarp = 2 * 16 * kBK * 4;             // 2 x (16 rows x 32 channels)
   static constexpr int kStage = 8 * kStageWarp;                   // 32 KiB output staging
-  static constexpr int kBytes = 2 * kWinBytes + kAStages * kA + kStage + 1024 + 256;
+  static constexpr int kBytes = kWinSlots * kWinBytes + kAStages * kA + kStage + 1024 + 256;
+  static_assert(kBytes <= 227 * 1024, "TN kernel shared memory over the per-CTA limit");
 };
 
 // Instances whose outputs leave through TMA tile stores staged in shared memory: the rows-mode
@@ -1133,23 +1141,25 @@ __global__ void __launch_bounds__(kTNThreads, 1)
                       const __grid_constant__ CUtensorMap tmO0,
                       const __grid_constant__ CUtensorMap tmO1, const ConvGeom g, const EpiParams e,
                       uint32_t *gerr) {
-  using P = TNCfg;
+  using P = TNCfg<F>;
   constexpr int AS = P::kAStages;
+  constexpr int WS = P::kWinSlots;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
-  const uint32_t win0 = base, ast0 = base + 2 * P::kWinBytes;
+  const uint32_t win0 = base, ast0 = base + WS * P::kWinBytes;
   const uint32_t stg0 = ast0 + AS * P::kA;   // epilogue output staging, kStageWarp per warp
   const uint32_t bar0 = stg0 + P::kStage;
   auto wfull = [&](int s) { return bar0 + 8u * s; };
-  auto wempty = [&](int s) { return bar0 + 8u * (2 + s); };
-  auto afull = [&](int s) { return bar0 + 8u * (4 + s); };   // accumulator ready
-  auto aempty = [&](int s) { return bar0 + 8u * (6 + s); };  // accumulator drained
-  auto sfull = [&](int s) { return bar0 + 8u * (8 + s); };   // weight stage loaded
-  auto sempty = [&](int s) { return bar0 + 8u * (8 + AS + s); };
-  const uint32_t dbar = bar0 + 8u * (8 + 2 * AS);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (9 + 2 * AS));
+  auto wempty = [&](int s) { return bar0 + 8u * (WS + s); };
+  auto afull = [&](int s) { return bar0 + 8u * (2 * WS + s); };       // accumulator ready
+  auto aempty = [&](int s) { return bar0 + 8u * (2 * WS + 2 + s); };  // accumulator drained
+  auto sfull = [&](int s) { return bar0 + 8u * (2 * WS + 4 + s); };   // weight stage loaded
+  auto sempty = [&](int s) { return bar0 + 8u * (2 * WS + 4 + AS + s); };
+  const uint32_t dbar = bar0 + 8u * (2 * WS + 4 + 2 * AS);
+  uint32_t *tmem_slot =
+      reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (2 * WS + 5 + 2 * AS));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1162,9 +1172,11 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   const int ntiles = g.tiles ? g.ntiles * mt : mt * tt * g.nbatch;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < WS; ++s) {
       mbar_init(wfull(s), 1);
       mbar_init(wempty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(afull(s), 1);
       mbar_init(aempty(s), 8);
     }
@@ -1192,7 +1204,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   if (warp == 8) {
     if (lane == 0) {
       // ---------------- TMA producer
-      int wiss[2] = {0, 0}, aiss[AS];
+      int wiss[WS] = {}, aiss[AS];
 #pragma unroll
       for (int s = 0; s < AS; ++s) aiss[s] = 0;
       bool ok = true;
@@ -1203,8 +1215,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         const int wlo = tl.r0 + g.row_off0 + lo_off;
         const int nbox = (tl.nr + wspan + kWinBox - 1) / kWinBox;
         for (int c = 0; c < kc && ok; ++c, ++cw) {
-          const int ws = cw & 1;
-          if (!mbar_wait(wempty(ws), ((cw >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+          const int ws = cw % WS;
+          if (!mbar_wait(wempty(ws), ((cw / WS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
             ok = false;
             break;
           }
@@ -1226,7 +1238,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         }
       }
       if (!ok) {
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < WS; ++s)
           if (wiss[s]) {
             uint32_t it = 0;
             while (!mbar_try_wait(wfull(s), (wiss[s] - 1) & 1) && ++it < kWaitLimit) {
@@ -1257,8 +1269,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + ab * kTNRows;
         for (int c = 0; c < kc && ok; ++c, ++cw) {
-          const int ws = cw & 1;
-          if (!mbar_wait(wfull(ws), (cw >> 1) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+          const int ws = cw % WS;
+          if (!mbar_wait(wfull(ws), (cw / WS) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
             ok = false;
             break;
           }
