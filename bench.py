@@ -53,6 +53,26 @@ SAMPLE_RATE = 16000
 HOP = 256
 
 
+_RESULT = None
+
+
+def own_stdout():
+    """The bench line is the only thing this program writes to stdout: it goes to a private copy
+    of the original stdout, and file descriptor 1 is pointed at stderr, so banners and logs of the
+    libraries (NCCL's version line, for one) never mix into it."""
+    global _RESULT
+    if _RESULT is None:
+        _RESULT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+        sys.stdout = sys.stderr
+
+
+def emit(obj):
+    out = _RESULT or sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -256,7 +276,7 @@ def traffic_from_csv(path):
                                  "(config 4, one decode)", "source": os.path.basename(path)}}
     with open(os.path.join(REPO, "profiles", "conv_tc_traffic.json"), "w") as f:
         json.dump(out, f, indent=1)
-    print(json.dumps(out))
+    emit(out)
     return 0
 
 
@@ -350,7 +370,7 @@ def reference_arm(args):
     tp = sorted(set(T[i] for i in picks))
     sample = (f"{len(picks)} config-4 requests per step (T in {tp[0]}..{tp[-1]}, the 16 shortest "
               f"cycled), one per host thread")
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * statistics.mean(times), 2), "higher_is_better": True,
@@ -360,13 +380,14 @@ def reference_arm(args):
                          "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }))
+    })
     return 0
 
 
 # ----------------------------------------------------------------------------------------------
 def main():
     args = parse()
+    own_stdout()
     if args.traffic_from:
         return traffic_from_csv(args.traffic_from)
     if args.impl == "reference":
@@ -413,7 +434,7 @@ def main():
     if args.profile_case:
         step_device()
         dec.sync(sh)
-        print(json.dumps({"profile_case": True, "requests": len(T), "frames": int(T.sum())}))
+        emit({"profile_case": True, "requests": len(T), "frames": int(T.sum())})
         return 0
 
     if args.layers:
@@ -612,7 +633,7 @@ def main():
     if world == 1 and not args.no_cpu_baseline and kind == "batch":
         out["cpu_baseline"] = cpu_baseline_block(T_all, zs_all, w)
     dec.close()
-    print(json.dumps(out))
+    emit(out)
     return 0
 
 
