@@ -83,16 +83,6 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   float *hf = reinterpret_cast<float *>(S.h);
   for (int i = threadIdx.x; i < 4 * 63; i += blockDim.x) hf[(i % 63) * 4 + i / 63] = a.pqmf[i];
   if (threadIdx.x < 16) S.win2[threadIdx.x] = c_win2[threadIdx.x];
-  // the output bin n of phase 1b is fixed per thread (the block size is a multiple of 16), so its
-  // basis column and window value live in registers
-  const int n = threadIdx.x & 15;
-  double bcn[9], bsn[9];
-#pragma unroll
-  for (int k = 0; k < 9; ++k) {
-    bcn[k] = c_bcd[k * 16 + n];
-    bsn[k] = c_bsd[k * 16 + n];
-  }
-  const float wn = c_win[n];
 
   // trimmed-OLA samples m needed by outputs [j0, j0 + W): stuffed index 4m in [j - 31, j + 31]
   long long m_lo = (j0 - 31 + 3) >> 2;
@@ -133,31 +123,36 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     }
   }
   __syncthreads();
-  // ---- 1b. per (frame, band, output bin): the 9 -> 16 basis sums in double, then the window
-  static_assert(kTailThreads % 16 == 0, "phase 1b keeps n = threadIdx.x % 16");
-  // two (frame, band) items a thread at a time: four independent double chains in flight
-  for (int it = threadIdx.x; it < NF * 64; it += 2 * blockDim.x) {
-    const int it2 = it + blockDim.x;
-    const bool two = it2 < NF * 64;
-    const int fl = it >> 6, b = (it >> 4) & 3;
-    const int fl2 = two ? it2 >> 6 : fl, b2 = (it2 >> 4) & 3;
-    double er = 0.0, ei = 0.0, er2 = 0.0, ei2 = 0.0;
-    // zero basis entries are skipped, as in the reference einsum.  Each product of two fp32
-    // values (24-bit significands) is exact in double, so one fused multiply-add rounds exactly
-    // where the reference's multiply-then-add does (its multiply is exact): the same bits.
+  // ---- 1b. per (frame, band, half of the 16 output bins): the 9 -> 16 basis sums in double,
+  // then the window.  A thread loads its frame's nine re / im values once and keeps 16
+  // independent chains (8 bins x re, im); items are grouped so that the 32 threads of a warp
+  // share the half, which makes every basis constant (and every zero skip) uniform across the
+  // warp.  Zero basis entries are skipped, as in the reference einsum, and each bin sums k in
+  // ascending order.  Each product of two fp32 values (24-bit significands) is exact in double,
+  // so one fused multiply-add rounds exactly where the reference's multiply-then-add does.
+  {
+    const int nfb = NF * 4, span = (nfb + 31) & ~31;   // (frame, band) items per half, padded
+    for (int it = threadIdx.x; it < 2 * span; it += blockDim.x) {
+      const int half = it >= span, fb = it - half * span;
+      if (fb >= nfb) continue;
+      const int fl = fb >> 2, b = fb & 3, n0 = half * 8;
+      double er[8], ei[8];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) {
-      if (bcn[k] != 0.0) {
-        er = __fma_rn(bcn[k], re[fl][b][k], er);
-        er2 = __fma_rn(bcn[k], re[fl2][b2][k], er2);
+      for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) {
+        const double rv = re[fl][b][k], iv = im[fl][b][k];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const double bc = c_bcd[k * 16 + n0 + j], bs = c_bsd[k * 16 + n0 + j];
+          if (bc != 0.0) er[j] = __fma_rn(bc, rv, er[j]);
+          if (bs != 0.0) ei[j] = __fma_rn(bs, iv, ei[j]);
+        }
       }
-      if (bsn[k] != 0.0) {
-        ei = __fma_rn(bsn[k], im[fl][b][k], ei);
-        ei2 = __fma_rn(bsn[k], im[fl2][b2][k], ei2);
-      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        fr[fl][b * 16 + n0 + j] = __fmul_rn(__fadd_rn((float)er[j], (float)ei[j]), c_win[n0 + j]);
     }
-    fr[fl][b * 16 + n] = __fmul_rn(__fadd_rn((float)er, (float)ei), wn);
-    if (two) fr[fl2][b2 * 16 + n] = __fmul_rn(__fadd_rn((float)er2, (float)ei2), wn);
   }
   __syncthreads();
 
