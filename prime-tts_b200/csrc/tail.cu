@@ -11,7 +11,8 @@
 //   3. x4 zero-stuffed upsampling with gain 4 (ConvTranspose_2) folded into the 63-tap PQMF
 //      synthesis conv: only taps landing on a stuffed sample (one in four) are evaluated.
 // Every fp32 step keeps the reference's operation order (no FMA contraction), so apart from the
-// exp/sin/cos implementations the tail reproduces the reference bit for bit.
+// exp/sin/cos implementations (and the sign of an exact-zero sample) the tail reproduces the
+// reference bit for bit.
 #include <cmath>
 #include <mutex>
 
@@ -53,13 +54,22 @@ struct TailArgs {
 
 __device__ __forceinline__ float tr_exp(float x, bool f32) { return f32 ? expf(x) : (float)exp((double)x); }
 __device__ __forceinline__ float tr_sin(float x, bool f32) { return f32 ? sinf(x) : (float)sin((double)x); }
-__device__ __forceinline__ float tr_cos(float x, bool f32) { return f32 ? cosf(x) : (float)cos((double)x); }
 // magnitude / phase of one bin: re = exp(a) * cos(pi * sin(b)), im = exp(a) * sin(pi * sin(b))
+// (the cosine and sine of the phase come from one sincos call: one argument reduction)
 __device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, float &iv) {
   const float mag = tr_exp(la, f32);
   const float ph = __fmul_rn(tr_sin(lb, f32), 3.1415927410125732f);
-  rv = __fmul_rn(mag, tr_cos(ph, f32));
-  iv = __fmul_rn(mag, tr_sin(ph, f32));
+  float c, sn;
+  if (f32) {
+    sincosf(ph, &sn, &c);
+  } else {
+    double sd, cd;
+    sincos((double)ph, &sd, &cd);
+    sn = (float)sd;
+    c = (float)cd;
+  }
+  rv = __fmul_rn(mag, c);
+  iv = __fmul_rn(mag, sn);
 }
 
 __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a) {
@@ -198,12 +208,14 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     for (int u = 0; u < 4; ++u) {
       const int i = j + 256 * u + k - 31;
       if (i < 0 || i >= nw) continue;
+      // the reference skips zero inputs; adding h x 0 instead changes a sum only in the sign of
+      // an exact zero, so no test is spent on them
       const float4 x4 = sm[(i >> 2) - mlo];
       float t = acc[u];
-      if (x4.x != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.x, x4.x));
-      if (x4.y != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.y, x4.y));
-      if (x4.z != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.z, x4.z));
-      if (x4.w != 0.0f) t = __fadd_rn(t, __fmul_rn(h4.w, x4.w));
+      t = __fadd_rn(t, __fmul_rn(h4.x, x4.x));
+      t = __fadd_rn(t, __fmul_rn(h4.y, x4.y));
+      t = __fadd_rn(t, __fmul_rn(h4.z, x4.z));
+      t = __fadd_rn(t, __fmul_rn(h4.w, x4.w));
       acc[u] = t;
     }
   }
