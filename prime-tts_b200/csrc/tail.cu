@@ -94,8 +94,10 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   for (int i = threadIdx.x; i < 4 * 63; i += blockDim.x) hf[(i % 63) * 4 + i / 63] = a.pqmf[i];
   if (threadIdx.x < 16) S.win2[threadIdx.x] = c_win2[threadIdx.x];
 
-  // trimmed-OLA samples m needed by outputs [j0, j0 + W): stuffed index 4m in [j - 31, j + 31]
-  long long m_lo = (j0 - 31 + 3) >> 2;
+  // trimmed-OLA samples m needed by outputs [j0, j0 + W): stuffed index 4m in [j - 31, j + 31];
+  // m_lo_raw .. m_hi_raw before clipping to the signal, which is zero outside [0, Ls)
+  const long long m_lo_raw = (j0 - 31 + 3) >> 2;
+  long long m_lo = m_lo_raw;
   if (m_lo < 0) m_lo = 0;
   long long m_hi = (j0 + kTailW - 1 + 31) >> 2;
   if (m_hi > Ls - 1) m_hi = Ls - 1;
@@ -166,10 +168,16 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   }
   __syncthreads();
 
-  // ---- 2. overlap-add / window-sum envelope, trimmed [8:-8]; frames outside [0, Tp) are absent
-  const int NM = (int)(m_hi - m_lo + 1);
-  for (int ml = threadIdx.x; ml < NM; ml += blockDim.x) {
-    const long long p = m_lo + ml + 8;
+  // ---- 2. overlap-add / window-sum envelope, trimmed [8:-8]; frames outside [0, Tp) are absent.
+  // sm[i] holds sample m_lo_raw + i; samples outside the signal (and the spare entries) are zero,
+  // so phase 3 reads its whole window without bounds tests.
+  for (int ml = threadIdx.x; ml < kTailM; ml += blockDim.x) {
+    const long long m = m_lo_raw + ml;
+    if (m < m_lo || m > m_hi) {
+      sm[ml] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      continue;
+    }
+    const long long p = m + 8;
     const long long q = p >> 2;
     const int r = (int)(p & 3);
     float ola[4] = {0.0f, 0.0f, 0.0f, 0.0f}, env = 0.0f;
@@ -190,39 +198,46 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   }
   __syncthreads();
 
-  // ---- 3. x4 zero-stuff (gain 4) + 63-tap PQMF synthesis, tap-major then band (conv order)
+  // ---- 3. x4 zero-stuff (gain 4) + 63-tap PQMF synthesis, tap-major then band (conv order).
+  // Polyphase: output j only meets taps k = k0 + 4s with (j + k - 31) divisible by 4.  A thread
+  // takes output phase p = j mod 4 and four consecutive outputs of that phase (j = j0 + 16g + 4v
+  // + p, v = 0..3); tap s of output v reads staged sample q0 + v + s, so the four outputs slide
+  // over one window and each tap loads one new sample and one filter tap.  Each output sums
+  // taps in ascending order, bands within a tap, as the reference conv does.
   float *wav = a.wav + (a.wav0 ? a.wav0[req] : 0);
   const int jn = (int)(nwav - j0 < kTailW ? nwav - j0 : kTailW);
-  const int mlo = (int)m_lo, nw = (int)nwav, jb = (int)j0;
   const int klo = (int)keep_lo, khi = (int)(keep_hi < nwav ? keep_hi : nwav);
-  // four outputs a thread, 256 apart: they share the tap phase k0 and every filter tap load, and
-  // keep four independent accumulation chains in flight; each output sums tap-major then band
-  static_assert(kTailW == 4 * kTailThreads, "phase 3 gives every thread four outputs");
-  const int j = jb + threadIdx.x;
-  const int k0 = (31 - j) & 3;   // first tap with (j + k - 31) % 4 == 0 (same for j + 256u)
+  static_assert(kTailW == 16 * kTailThreads / 4, "phase 3 gives every thread four outputs");
+  const int p = threadIdx.x & 3, g = threadIdx.x >> 2;
+  const int k0 = (31 - p) & 3, ntap = (63 - k0 + 3) >> 2;
+  // j0 is a multiple of 4, so j + k0 - 31 is: the shift divides exactly
+  const int q0 = (int)(((j0 + 16 * g + p + k0 - 31) >> 2) - m_lo_raw);
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float4 x0 = sm[q0], x1 = sm[q0 + 1], x2 = sm[q0 + 2], x3 = sm[q0 + 3];
+  auto tap = [](float t, const float4 h, const float4 x) {
+    t = __fadd_rn(t, __fmul_rn(h.x, x.x));
+    t = __fadd_rn(t, __fmul_rn(h.y, x.y));
+    t = __fadd_rn(t, __fmul_rn(h.z, x.z));
+    return __fadd_rn(t, __fmul_rn(h.w, x.w));
+  };
+  // (the reference skips zero inputs; adding h x 0 changes a sum only in the sign of an exact zero)
 #pragma unroll 4
-  for (int k = k0; k < 63; k += 4) {
-    const float4 h4 = S.h[k];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = j + 256 * u + k - 31;
-      if (i < 0 || i >= nw) continue;
-      // the reference skips zero inputs; adding h x 0 instead changes a sum only in the sign of
-      // an exact zero, so no test is spent on them
-      const float4 x4 = sm[(i >> 2) - mlo];
-      float t = acc[u];
-      t = __fadd_rn(t, __fmul_rn(h4.x, x4.x));
-      t = __fadd_rn(t, __fmul_rn(h4.y, x4.y));
-      t = __fadd_rn(t, __fmul_rn(h4.z, x4.z));
-      t = __fadd_rn(t, __fmul_rn(h4.w, x4.w));
-      acc[u] = t;
-    }
+  for (int s = 0; s < ntap; ++s) {
+    const float4 h4 = S.h[k0 + 4 * s];
+    acc[0] = tap(acc[0], h4, x0);
+    acc[1] = tap(acc[1], h4, x1);
+    acc[2] = tap(acc[2], h4, x2);
+    acc[3] = tap(acc[3], h4, x3);
+    x0 = x1;
+    x1 = x2;
+    x2 = x3;
+    x3 = sm[q0 + s + 4];
   }
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int jj = threadIdx.x + 256 * u, ju = j + 256 * u;
-    if (jj < jn && ju >= klo && ju < khi) wav[ju] = acc[u];
+  for (int v = 0; v < 4; ++v) {
+    const int jj = 16 * g + 4 * v + p;
+    const long long ju = j0 + jj;
+    if (jj < jn && ju >= klo && ju < khi) wav[ju] = acc[v];
   }
 }
 
