@@ -241,9 +241,26 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   }
   PTB_REQUIRE(!L.g.tiles || (L.batch == 1 && L.g.ntiles > 0),
               "pt_b200: a conv tile list needs batch 1 and at least one tile");
-  const long long tiles = (long long)((L.g.n_cols + kBM - 1) / kBM) *
-                          (L.g.tiles ? L.g.ntiles : ((L.g.m_rows + kTNRows - 1) / kTNRows) * L.batch);
   ConvGeom g = L.g;
+  const long long mtl = (L.g.n_cols + kBM - 1) / kBM;
+  g.tile_rows = kTNRows;
+  static int pick = -1;
+  if (pick < 0) pick = getenv("PT_B200_TILE_PICK") ? atoi(getenv("PT_B200_TILE_PICK")) : 1;
+  if (!L.g.tiles && pick) {
+    // The tile height whose last wave is fullest: waves x (rows + a per-tile cost of 16 rows,
+    // the weight stream and pipeline fill) over heights 256 .. 160.
+    long long best = -1;
+    for (int h = kTNRows; h >= 160; h -= 16) {
+      const long long n = mtl * ((L.g.m_rows + h - 1) / h) * L.batch;
+      const long long cost = ((n + sms - 1) / sms) * (h + 16);
+      if (best < 0 || cost < best) {
+        best = cost;
+        g.tile_rows = h;
+      }
+    }
+  }
+  const long long tiles =
+      mtl * (L.g.tiles ? L.g.ntiles : ((L.g.m_rows + g.tile_rows - 1) / g.tile_rows) * L.batch);
   g.nbatch = L.batch;
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
   conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg<F>::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);

@@ -51,6 +51,9 @@ struct ConvGeom {
   // Channels-on-M kernel only: walk the tiles last to first, so that a layer starts on the rows
   // its producer wrote last (still in L2); the decoder alternates it between layers.
   int reverse;
+  // Channels-on-M kernel only: rows per tile of the uniform schedule (a multiple of 16, <= 256;
+  // 0 = 256), chosen by the launcher so that the last wave of tiles is nearly full.
+  int tile_rows;
 };
 
 struct EpiParams {
@@ -930,11 +933,12 @@ __device__ __forceinline__ TNTile tn_tile(const ConvGeom &g, int t, int mt, int 
     x.r0 = v.x;
     x.nr = v.y;
   } else {
+    const int h = g.tile_rows ? g.tile_rows : kTNRows;
     x.z = t / (mt * tt);
     const int r = t - x.z * mt * tt, ti = r / mt;
     x.mi = r - ti * mt;
-    x.r0 = ti * kTNRows;
-    x.nr = kTNRows;
+    x.r0 = ti * h;
+    x.nr = h;
   }
   return x;
 }
@@ -1168,7 +1172,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   const int lo_off = span < 0 ? span : 0;
   const int wspan = span < 0 ? -span : span;
   const int mt = (g.n_cols + kBM - 1) / kBM;              // channel tiles (fastest)
-  const int tt = (g.m_rows + kTNRows - 1) / kTNRows;      // time tiles
+  const int th = g.tile_rows ? g.tile_rows : kTNRows;
+  const int tt = (g.m_rows + th - 1) / th;                 // time tiles
   const int ntiles = g.tiles ? g.ntiles * mt : mt * tt * g.nbatch;
 
   if (threadIdx.x == 0) {
