@@ -141,3 +141,12 @@ def test_carry_plan_rejects_bad_arguments():
         Ta = np.ascontiguousarray(T, np.int64)
         assert pt_b200.lib().pt_b200_carry_plan(len(Ta), Ta.ctypes.data_as(pt_b200._i64p), chunk,
                                                 None, None, 0) == -1
+
+
+def test_carry_plan_rejects_sessions_past_the_32_bit_row_limit():
+    """Epilogue offsets are 32-bit: a session whose level-2 tensors would pass 2^31 elements is
+    refused by the planner with a message, before any device memory is touched."""
+    T = np.full(2000, 600, np.int64)   # 1.2M frames: ~19M level-2 rows x 128 channels
+    n = pt_b200.lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(pt_b200._i64p), 32, None, None, 0)
+    assert n == -1
+    assert b"too large" in pt_b200.lib().pt_b200_last_error()
