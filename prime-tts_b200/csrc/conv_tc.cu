@@ -5,6 +5,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #define PTB_CONV_KERNELS
 #include "common.cuh"
@@ -107,17 +109,25 @@ struct StagesFor {
   static constexpr int value = BN >= 256 ? 4 : BN >= 128 ? 6 : 8;
 };
 
+// A kernel's opt-in to more than 48 KB of dynamic shared memory belongs to the device it was
+// made on: make it once per (kernel, device), on the calling thread's current device.
+static int smem_optin(const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void *, int>> done;
+  int dev = 0;
+  PTB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kernel, dev})) return 0;
+  PTB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({kernel, dev});
+  return 0;
+}
+
 template <int BN>
 static int launch_bn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   constexpr int S = StagesFor<BN>::value;
   constexpr int smem = ConvSmem<BN, S>::kBytes;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(conv_tc_kernel<BN, S>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  });
-  PTB_CUDA(attr_err);
+  if (smem_optin(reinterpret_cast<const void *>(conv_tc_kernel<BN, S>), smem)) return -1;
   CUtensorMap ta, tb;
   if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kBM)) return -1;
   if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
@@ -132,13 +142,8 @@ static int launch_bn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
 template <int BN, int MSUB>
 static int launch_win(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   using W = WinCfg<BN, MSUB>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(conv_tc_win_kernel<BN, MSUB>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, W::kBytes);
-  });
-  PTB_CUDA(attr_err);
+  if (smem_optin(reinterpret_cast<const void *>(conv_tc_win_kernel<BN, MSUB>), W::kBytes))
+    return -1;
   CUtensorMap ta, tb;
   if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
   if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
@@ -181,13 +186,7 @@ static int pick_msub(const ConvLaunch &L, const int *cands, int ncand) {
 template <int BN>
 static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   using P = PersCfg<BN>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(conv_tc_pers_kernel<BN>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, P::kBytes);
-  });
-  PTB_CUDA(attr_err);
+  if (smem_optin(reinterpret_cast<const void *>(conv_tc_pers_kernel<BN>), P::kBytes)) return -1;
   static int sms = 0;
   if (!sms) {
     int dev = 0;
@@ -211,20 +210,10 @@ static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
 
 template <int MODE, int F>
 static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
-  // the shared-memory opt-in is per device
-  static std::mutex mu;
-  static unsigned long long attr_done = 0;
+  if (smem_optin(reinterpret_cast<const void *>(conv_tc_tn_kernel<MODE, F>), TNCfg<F>::kBytes))
+    return -1;
   int dev = 0;
   PTB_CUDA(cudaGetDevice(&dev));
-  PTB_REQUIRE(dev >= 0 && dev < 64, "pt_b200: device index %d out of range", dev);
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!((attr_done >> dev) & 1ull)) {
-      PTB_CUDA(cudaFuncSetAttribute(conv_tc_tn_kernel<MODE, F>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, TNCfg<F>::kBytes));
-      attr_done |= 1ull << dev;
-    }
-  }
   static int sms = 0;
   if (!sms) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -84,3 +84,37 @@ def test_two_gloo_ranks_match_single_rank():
     assert sorted(got) == list(range(len(T)))
     for i in range(len(T)):
         assert np.array_equal(np.asarray(got[i], np.float32), cpu.decode(w, zs[i]))
+
+
+def _gpu_count():
+    try:
+        import torch
+        return torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:
+        return 0
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_interpreter_contexts_on_two_devices_agree():
+    """Request-parallel interpreter use: a context bound to device 1 (pt_v21_cuda_init_dev) runs
+    the same convs as one on device 0 -- a small-N conv (the window kernel) and a 256-channel
+    conv (the channels-on-M kernel), each kernel's shared-memory opt-in made on each device --
+    and returns the same bits."""
+    import pt_b200
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((1, 128, 300)).astype(np.float32)
+    cases = [(48, 7, 3), (256, 3, 1)]
+    outs = {}
+    for dev in (0, 1):
+        with pt_b200.Context(device=dev) as ctx:
+            res = []
+            for cout, K, pad in cases:
+                W = (0.02 * rng.standard_normal((cout, 128, K))).astype(np.float32) if dev == 0 \
+                    else outs[("w", cout)]
+                outs[("w", cout)] = W
+                b = np.zeros(cout, np.float32)
+                res.append(ctx.conv(x, pt_b200.pack_conv(W), b, cout=cout, K=K, pad=pad))
+            outs[dev] = res
+    for a, b in zip(outs[0], outs[1]):
+        np.testing.assert_array_equal(a, b)
