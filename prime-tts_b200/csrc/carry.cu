@@ -243,6 +243,7 @@ int run_pass(pt_b200_carry *c, cudaStream_t st, int k, const float *z_dev, float
       e.obase = s == 0 ? p.ob01 : p.ob12;
       e.s = 4;
       e.cphase = C;
+      e.out_rows = (int)rout;
       e.out0 = c->U[s];
       e.out1 = c->LU[s];
       if (conv(d->ups[s], lvl_in, rin, 0, -1, e)) return -1;

@@ -101,6 +101,26 @@ int make_map_out(CUtensorMap *m, const float *base, int ld, int64_t rows) {
   return 0;
 }
 
+// Output map of the upsampler epilogue: [rows][ld] fp32 viewed as (ld, 4, rows / 4), so that
+// rows 4q + p for 16 consecutive q (one phase p) are one 32-channel x 1 x 16 box.
+static int make_map_out_convt(CUtensorMap *m, const float *base, int ld, int64_t rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (encoder(&enc)) return -1;
+  PTB_REQUIRE(base && (reinterpret_cast<uintptr_t>(base) & 15) == 0 && ld % kBK == 0 && rows > 0 &&
+                  rows % 4 == 0,
+              "pt_b200: upsampler output map needs a 16-byte aligned base, 32-channel rows and "
+              "a multiple of 4 rows");
+  cuuint64_t dims[3] = {(cuuint64_t)ld, 4, (cuuint64_t)(rows / 4)};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * 16};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, 1, 16};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PTB_REQUIRE(r == CUDA_SUCCESS, "pt_b200: upsampler output map encode failed (%d)", (int)r);
+  return 0;
+}
+
 // ---------------------------------------------------------------------------- instances
 // N tiles compiled: the decoder needs 256 (256/512-channel layers, upsamplers), 128 (128-channel
 // layers) and 80 (conv_post, 72 channels); 16/32/64 serve the small tail convs and generic calls.
@@ -227,6 +247,11 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   if constexpr (TNTmaStore<MODE, F>::value) {
     if ((F & EF_OUT0) && make_map_out(&to0, L.e.out0, L.e.ldc, L.g.m_rows)) return -1;
     if ((F & EF_OUT1) && make_map_out(&to1, L.e.out1, L.e.ldc1, L.g.m_rows)) return -1;
+  }
+  if constexpr (TNConvTStore<MODE, F>::value) {
+    if (make_map_out_convt(&to0, L.e.out0, L.e.ldc, L.e.out_rows) ||
+        make_map_out_convt(&to1, L.e.out1, L.e.ldc1, L.e.out_rows))
+      return -1;
   }
   PTB_REQUIRE(!L.g.tiles || (L.batch == 1 && L.g.ntiles > 0),
               "pt_b200: a conv tile list needs batch 1 and at least one tile");

@@ -80,6 +80,7 @@ struct EpiParams {
   int acc_mode;               // 0 none, 2: v = accin + v, 3: v = (accin + v) / 3
   float alpha1;
   int refl;                   // rows marked bit1 in mask are also written to row - 2
+  int out_rows;               // convT: rows of out0 / out1 (a multiple of 4; the TMA-store view)
 };
 
 // Compile-time shape of a decoder epilogue (the TN kernel is instantiated per combination, so
@@ -947,6 +948,13 @@ template <int MODE, int F>
 struct TNTmaStore {
   static constexpr bool value = MODE == EPI_ROWS && F != EF_GENERIC;
 };
+// The upsampler instance (out0 + out1) stores a pass whose 16 delay-line steps all map into one
+// request -- output rows 4 apart, one phase per warp -- as one TMA tile through a (C, 4, rows/4)
+// view of each output; other passes (a request boundary inside) store directly.
+template <int MODE, int F>
+struct TNConvTStore {
+  static constexpr bool value = MODE == EPI_ROWS_CONVT && F == (EF_OUT0 | EF_OUT1);
+};
 
 // Plain-mode (interpreter ABI) epilogue of one 32-channel x 32-row block: this thread's channel
 // n, time rows t0..t0+31, read from TMEM at `taddr` (D[n][t0 + i] -> column i).  Rows at or past
@@ -1112,6 +1120,35 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
     }
     slot ^= 1;
     return;
+  }
+  if constexpr (TNConvTStore<MODE, F>::value) {
+    const int li = lane & 15;
+    const int myrow = __shfl_sync(0xffffffffu, orow_blk, 16 * h + li);
+    const int row0 = __shfl_sync(0xffffffffu, orow_blk, 16 * h);
+    if (__all_sync(0xffffffffu, myrow >= 0 && myrow == row0 + 4 * li)) {
+      const int col0 = col - lane;
+      float v[16];
+      tmem_ld16(taddr, v);
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+      const uint32_t s0 = stage, s1 = stage + 16 * kBK * 4;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const bool ok = ((vh >> i) & 1) && colok;
+        const float x = v[i] + bias;
+        const uint32_t at = static_cast<uint32_t>(i * kBK * 4 + lane * 4);
+        st_shared_f32(s0 + at, ok ? x : 0.0f);
+        st_shared_f32(s1 + at, ok ? tf32_rna(leaky(x, e.alpha1)) : 0.0f);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && col0 < e.nstore) {
+        tma_store_3d(tm0, s0, col0, row0 & 3, row0 >> 2);
+        tma_store_3d(tm1, s1, col0, row0 & 3, row0 >> 2);
+        bulk_commit();
+      }
+      return;
+    }
   }
   const unsigned rh =
       hrefl ? (__ballot_sync(0xffffffffu, (mk >> 1) & 1u) >> (16 * h)) & 0xffffu : 0u;
@@ -1380,7 +1417,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(aempty(ab));
     }
-    if constexpr (TNTmaStore<MODE, F>::value) {
+    if constexpr (TNTmaStore<MODE, F>::value || TNConvTStore<MODE, F>::value) {
       if (lane == 0) bulk_wait_all();   // staged stores done before the CTA's memory goes
       __syncwarp();
     }

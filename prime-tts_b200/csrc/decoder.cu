@@ -2,9 +2,10 @@
 //
 // Ragged batch layout.  At each time resolution (level 0: latent frames T, level 1: 4T after
 // ups.0, level 2: 16T after ups.1) the requests are stacked along time in one channels-last
-// tensor [rows][C], each request's rows preceded and followed by zero gap rows: 8 at level 0
-// (conv_pre reaches 3 rows, ups.0 reads 2 before and 1 after a request), 28 at level 1 and 32 at
-// level 2 (the widest conv reaches dilation 5 x (11-1)/2 = 25 rows; conv_post reads 3 + 1
+// tensor [rows][C], each request's rows preceded and followed by zero gap rows: 16 at level 0
+// (conv_pre reaches 3 rows, ups.0 reads 2 before and 1 after a request; 16 so that a 16-row
+// epilogue slab rounded outward from one request never reaches the next), 28 at level 1 and 32
+// at level 2 (the widest conv reaches dilation 5 x (11-1)/2 = 25 rows; conv_post reads 3 + 1
 // reflection row).  So one launch per layer computes every request exactly as if it ran
 // alone: the zero gap rows are the convolutions' zero padding, and the epilogue never writes them
 // (a per-row mask), so they stay zero.
@@ -348,6 +349,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
       e.obase = s == 0 ? p.ob01 : p.ob12;
       e.s = 4;
       e.cphase = C;
+      e.out_rows = (int)rout;
       e.out0 = d->U[s];
       e.out1 = d->LU[s];
       if (run_conv(d, st, d->ups[s], lvl_in, rin, 0, -1, e, nullptr, 0, rev())) return -1;
