@@ -83,6 +83,8 @@ def parse():
                     help="skip the CPU baseline leg (used for profiler passes)")
     ap.add_argument("--profile-case", action="store_true",
                     help="one untimed device decode of the workload, for ncu captures")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="with --profile-case: decode only the first N requests (a small case)")
     ap.add_argument("--workload", choices=["batch", "stream"], default="batch",
                     help="batch: config 4 (default); stream: config 5")
     ap.add_argument("--stream-scheme", choices=["carry", "windows"], default="carry",
@@ -407,6 +409,8 @@ def main():
 
     kind = args.workload
     T_all, zs_all, w = workload(world, kind)
+    if args.profile_case and args.requests > 0:
+        T_all, zs_all = T_all[:args.requests], zs_all[:args.requests]
     shard = lpt_shards(T_all, world)[rank]
     T = np.array([T_all[i] for i in shard], np.int64)
     zcat = np.concatenate([zs_all[i].ravel() for i in shard])
