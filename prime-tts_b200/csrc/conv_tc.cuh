@@ -895,20 +895,29 @@ __global__ void __launch_bounds__(kPThreads, 1)
 // accumulator sets (2 x 256 columns), channel blocks fastest so consecutive tiles reuse the same
 // activation window from L2.
 constexpr int kTNRows = 256;    // time rows per tile (MMA N)
-constexpr int kTNThreads = 320; // warps 0-7 epilogue, 8 TMA producer, 9 TMEM allocator + MMA
+// warps 0-7 epilogue, 8 activation-window producer, 9 TMEM allocator + MMA, 10 weight producer
+constexpr int kTNThreads = 352;
 
-// Pipeline shape.  The convs1 instances (no residual) are tensor-bound: 2 activation-window slots
-// and 7 weight stages.  The residual-reading convs2 instances trade weight stages for a third
-// window slot, which keeps their window loads further ahead of the MMAs while the epilogue's
-// residual reads load the memory system (3-12 us a layer on config 4; the convs1 layers lose
-// 2-6 us with fewer weight stages, so they keep 7).
+// Pipeline shape.  Windows and weight stages come from two producer warps, so each ring runs
+// ahead of the MMAs by its own depth: a k = 3 layer consumes a 32-channel window in three weight
+// stages (~0.8 us of MMA), less than one window's DRAM latency plus transfer, and needs windows
+// two chunks ahead whatever the weight ring holds.  With one producer issuing both in order, the
+// weight ring capped the window lead at about one chunk.  On config 4: 5,445 -> 5,327 us per
+// decode summed over the layers (256-channel k3 convs2 94 -> 84 us); three window slots with four
+// weight stages beat two with seven (5,357) and four with two (6,428, weight-starved).
+#ifndef PTB_TN_WIN_SLOTS
+#define PTB_TN_WIN_SLOTS 3
+#endif
+#ifndef PTB_TN_A_STAGES
+#define PTB_TN_A_STAGES 4
+#endif
 template <int F>
 struct TNCfg {
-  static constexpr int kWinSlots = (F != EF_GENERIC && (F & EF_RES)) ? 3 : 2;
+  static constexpr int kWinSlots = PTB_TN_WIN_SLOTS;
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
-  static constexpr int kAStages = kWinSlots == 3 ? 4 : 7;
+  static constexpr int kAStages = PTB_TN_A_STAGES;
   static constexpr int kStageWarp = 2 * 16 * kBK * 4;             // 2 x (16 rows x 32 channels)
   static constexpr int kStage = 8 * kStageWarp;                   // 32 KiB output staging
   static constexpr int kBytes = kWinSlots * kWinBytes + kAStages * kA + kStage + 1024 + 256;
@@ -1245,18 +1254,16 @@ __global__ void __launch_bounds__(kTNThreads, 1)
 
   if (warp == 8) {
     if (lane == 0) {
-      // ---------------- TMA producer
-      int wiss[WS] = {}, aiss[AS];
-#pragma unroll
-      for (int s = 0; s < AS; ++s) aiss[s] = 0;
+      // ---------------- TMA producer: activation windows (one per 32-channel chunk)
+      int wiss[WS] = {};
       bool ok = true;
-      int cw = 0, ca = 0;
+      int cw = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const TNTile tl = tn_tile(g, t, mt, tt, ntiles);
-        const int z = tl.z, mi = tl.mi;
+        const int z = tl.z;
         const int wlo = tl.r0 + g.row_off0 + lo_off;
         const int nbox = (tl.nr + wspan + kWinBox - 1) / kWinBox;
-        for (int c = 0; c < kc && ok; ++c, ++cw) {
+        for (int c = 0; c < kc; ++c, ++cw) {
           const int ws = cw % WS;
           if (!mbar_wait(wempty(ws), ((cw / WS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
             ok = false;
@@ -1267,6 +1274,28 @@ __global__ void __launch_bounds__(kTNThreads, 1)
           for (int b = 0; b < nbox; ++b)
             tma_load_3d(wb + b * kWinBox * kBK * 4, &tmX, wfull(ws), c * kBK, wlo + b * kWinBox, z);
           ++wiss[ws];
+        }
+      }
+      if (!ok)
+        for (int s = 0; s < WS; ++s)
+          if (wiss[s]) {
+            uint32_t it = 0;
+            while (!mbar_try_wait(wfull(s), (wiss[s] - 1) & 1) && ++it < kWaitLimit) {
+            }
+            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
+          }
+    }
+  } else if (warp == 10) {
+    if (lane == 0) {
+      // ---------------- TMA producer: weight stages (one per chunk and tap)
+      int aiss[AS];
+#pragma unroll
+      for (int s = 0; s < AS; ++s) aiss[s] = 0;
+      bool ok = true;
+      int ca = 0;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int mi = tn_tile(g, t, mt, tt, ntiles).mi;
+        for (int c = 0; c < kc && ok; ++c)
           for (int k = 0; k < g.ntap; ++k, ++ca) {
             const int as = ca % AS;
             if (!mbar_wait(sempty(as), ((ca / AS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
@@ -1277,16 +1306,8 @@ __global__ void __launch_bounds__(kTNThreads, 1)
             tma_load_2d(ast0 + as * P::kA, &tmW, sfull(as), k * g.cin32 + c * kBK, mi * kBM);
             ++aiss[as];
           }
-        }
       }
-      if (!ok) {
-        for (int s = 0; s < WS; ++s)
-          if (wiss[s]) {
-            uint32_t it = 0;
-            while (!mbar_try_wait(wfull(s), (wiss[s] - 1) & 1) && ++it < kWaitLimit) {
-            }
-            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
-          }
+      if (!ok)
         for (int s = 0; s < AS; ++s)
           if (aiss[s]) {
             uint32_t it = 0;
@@ -1294,7 +1315,6 @@ __global__ void __launch_bounds__(kTNThreads, 1)
             }
             if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
           }
-      }
     }
   } else if (warp == 9) {
     if (lane == 0) {
