@@ -1319,10 +1319,22 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   } else if (warp == 9) {
     if (lane == 0) {
       // ---------------- MMA issuer: M = 128 channels, N = the tile's time rows (<= 256)
+      // The tensor pipe queues few MMAs, so every instruction this thread spends between two
+      // MMAs beyond one MMA's duration idles it: descriptors advance by adds (the address field
+      // is the shared-memory byte address / 16), ring slots and phases are counters, and the
+      // next tile's height is read while this tile's MMAs run.
       bool ok = true;
-      int cw = 0, ca = 0, it = 0;
+      int it = 0, ws = 0, as = 0;
+      uint32_t wph = 0, aph = 0;
+      const uint64_t dA0 = sdesc_kmajor_sw128(ast0);
+      const uint64_t dW0 = sdesc_kmajor_sw128(win0 + static_cast<uint32_t>(-lo_off) * (kBK * 4));
+      const int64_t dtap = static_cast<int64_t>(g.row_step) * (kBK * 4 / 16);
+      const int ntap = g.ntap;
+      int nr = blockIdx.x < ntiles ? tn_tile(g, blockIdx.x, mt, tt, ntiles).nr : 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-        const uint32_t idesc = idesc_tf32(kBM, tn_tile(g, t, mt, tt, ntiles).nr);
+        const uint32_t idesc = idesc_tf32(kBM, nr);
+        if (t + static_cast<int>(gridDim.x) < ntiles)
+          nr = tn_tile(g, t + gridDim.x, mt, tt, ntiles).nr;
         const int ab = it & 1;
         if (!mbar_wait(aempty(ab), ((it >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
           ok = false;
@@ -1330,29 +1342,37 @@ __global__ void __launch_bounds__(kTNThreads, 1)
         }
         tc_fence_after();
         const uint32_t acc = tmem + ab * kTNRows;
-        for (int c = 0; c < kc && ok; ++c, ++cw) {
-          const int ws = cw % WS;
-          if (!mbar_wait(wfull(ws), (cw / WS) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+        uint32_t accum = 0;
+        for (int c = 0; c < kc && ok; ++c) {
+          if (!mbar_wait(wfull(ws), wph, abort_flag, gerr, ERR_WAIT_FULL)) {
             ok = false;
             break;
           }
-          const uint32_t wb = win0 + ws * P::kWinBytes;
-          for (int k = 0; k < g.ntap; ++k, ++ca) {
-            const int as = ca % AS;
-            if (!mbar_wait(sfull(as), (ca / AS) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
+          uint64_t dB = dW0 + static_cast<uint64_t>(ws * (P::kWinBytes / 16));
+          for (int k = 0; k < ntap; ++k) {
+            if (!mbar_wait(sfull(as), aph, abort_flag, gerr, ERR_WAIT_FULL)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t da = sdesc_kmajor_sw128(ast0 + as * P::kA);
-            const uint64_t db =
-                sdesc_kmajor_sw128(wb + (uint32_t)(k * g.row_step - lo_off) * (kBK * 4));
-#pragma unroll
-            for (int kk = 0; kk < kBK / 8; ++kk)
-              mma_tf32(acc, da + 2u * kk, db + 2u * kk, idesc, (c | k | kk) != 0);
+            const uint64_t dA = dA0 + static_cast<uint64_t>(as * (P::kA / 16));
+            mma_tf32(acc, dA, dB, idesc, accum);
+            mma_tf32(acc, dA + 2u, dB + 2u, idesc, 1u);
+            mma_tf32(acc, dA + 4u, dB + 4u, idesc, 1u);
+            mma_tf32(acc, dA + 6u, dB + 6u, idesc, 1u);
+            accum = 1u;
             mma_commit(sempty(as));
+            if (++as == AS) {
+              as = 0;
+              aph ^= 1u;
+            }
+            dB += static_cast<uint64_t>(dtap);
           }
           if (ok) mma_commit(wempty(ws));
+          if (++ws == WS) {
+            ws = 0;
+            wph ^= 1u;
+          }
         }
         if (ok) mma_commit(afull(ab));
       }
