@@ -218,9 +218,13 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 }
 
 // fp32 -> tf32 with round-to-nearest (ties away), the value kept in an fp32 container.
+// Integer form: add half of the 13 dropped mantissa bits to the magnitude and truncate (ties go
+// away from zero; a mantissa carry moves into the exponent).  Inf and NaN pass unchanged.  It is
+// the epilogues' per-element conversion, so it stays on the integer pipe: the conversion
+// instruction's lower throughput showed up as the largest part of an epilogue pass.
 __device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  const uint32_t b = __float_as_uint(x);
+  const uint32_t r = (b & 0x7f800000u) == 0x7f800000u ? b : (b + 0x1000u) & 0xffffe000u;
   return __uint_as_float(r);
 }
 
