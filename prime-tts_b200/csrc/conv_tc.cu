@@ -277,7 +277,7 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
       mtl * (L.g.tiles ? L.g.ntiles : ((L.g.m_rows + g.tile_rows - 1) / g.tile_rows) * L.batch);
   g.nbatch = L.batch;
   const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  conv_tc_tn_kernel<MODE, F><<<grid, kTNThreads, TNCfg<F>::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);
+  conv_tc_tn_kernel<MODE, F><<<grid, TNCfg<F>::kThreads, TNCfg<F>::kBytes, st>>>(tx, tw, to0, to1, g, L.e, gerr);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;

@@ -895,8 +895,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 // accumulator sets (2 x 256 columns), channel blocks fastest so consecutive tiles reuse the same
 // activation window from L2.
 constexpr int kTNRows = 256;    // time rows per tile (MMA N)
-// warps 0-7 epilogue, 8 activation-window producer, 9 TMEM allocator + MMA, 10 weight producer
-constexpr int kTNThreads = 352;
+// Warps 0 .. E-1 epilogue (E = TNCfg<F>::kEpiWarps), E activation-window producer, E+1 TMEM
+// allocator + MMA issuer, E+2 weight producer.
 
 // Pipeline shape.  Windows and weight stages come from two producer warps, so each ring runs
 // ahead of the MMAs by its own depth: a k = 3 layer consumes a 32-channel window in three weight
@@ -918,8 +918,15 @@ struct TNCfg {
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
   static constexpr int kAStages = PTB_TN_A_STAGES;
-  static constexpr int kStageWarp = 2 * 16 * kBK * 4;             // 2 x (16 rows x 32 channels)
-  static constexpr int kStage = 8 * kStageWarp;                   // 32 KiB output staging
+  // Single-output instances without residual or branch-sum inputs (conv_pre, convs1, conv_post)
+  // run 16 epilogue warps of one staging slot each: their epilogue is a chain of short dependent
+  // steps per 16-row pass, and on the 128-channel k = 3 layers it, not the MMA, sets the pace;
+  // twice the warps hide twice the latency in the same registers and shared memory.
+  static constexpr int kEpiWarps = (F == EF_OUT1 || F == EF_OUT0) ? 16 : 8;
+  static constexpr int kThreads = 32 * (kEpiWarps + 3);
+  static constexpr int kSlots = kEpiWarps == 16 ? 1 : 2;          // staging slots per warp
+  static constexpr int kStageWarp = kSlots * 16 * kBK * 4;        // slots x (16 rows x 32 channels)
+  static constexpr int kStage = kEpiWarps * kStageWarp;           // 32 KiB output staging
   static constexpr int kBytes = kWinSlots * kWinBytes + kAStages * kA + kStage + 1024 + 256;
   static_assert(kBytes <= 227 * 1024, "TN kernel shared memory over the per-CTA limit");
 };
@@ -1076,15 +1083,17 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
   if (!vh) return;   // uniform over the warp: nothing of this pass is stored
   if constexpr (TNTmaStore<MODE, F>::value) {
     constexpr bool two = (F & EF_OUT0) && (F & EF_OUT1);
+    constexpr bool one_slot = TNCfg<F>::kSlots == 1;
     const int col0 = col - lane;
     float v[16];
     tmem_ld16(taddr, v);
     if (lane == 0) {
-      if (two) bulk_wait_read<0>();
+      if (two || one_slot) bulk_wait_read<0>();
       else bulk_wait_read<1>();
     }
     __syncwarp();
-    const uint32_t s0 = stage + (two ? 0u : static_cast<uint32_t>(slot) * (16 * kBK * 4));
+    const uint32_t s0 =
+        stage + (two || one_slot ? 0u : static_cast<uint32_t>(slot) * (16 * kBK * 4));
     const uint32_t s1 = two ? stage + 16 * kBK * 4 : s0;
     if constexpr ((F & EF_REFL) != 0) {
       // out1 only: rows whose mask has bit 2 take the value of the row two below (same pass)
@@ -1186,7 +1195,7 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
 }
 
 template <int MODE, int F>
-__global__ void __launch_bounds__(kTNThreads, 1)
+__global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
     conv_tc_tn_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                       const __grid_constant__ CUtensorMap tmO0,
                       const __grid_constant__ CUtensorMap tmO1, const ConvGeom g, const EpiParams e,
@@ -1194,6 +1203,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   using P = TNCfg<F>;
   constexpr int AS = P::kAStages;
   constexpr int WS = P::kWinSlots;
+  constexpr int EW = P::kEpiWarps;   // epilogue warps; then the window producer, MMA, weights
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1229,7 +1239,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(afull(s), 1);
-      mbar_init(aempty(s), 8);
+      mbar_init(aempty(s), EW);
     }
     for (int s = 0; s < AS; ++s) {
       mbar_init(sfull(s), 1);
@@ -1239,11 +1249,11 @@ __global__ void __launch_bounds__(kTNThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == EW && lane == 0) {
     prefetch_tmap(&tmX);
     prefetch_tmap(&tmW);
   }
-  if (warp == 9) {
+  if (warp == EW + 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -1252,7 +1262,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == EW) {
     if (lane == 0) {
       // ---------------- TMA producer: activation windows (one per 32-channel chunk)
       int wiss[WS] = {};
@@ -1285,7 +1295,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
             if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
           }
     }
-  } else if (warp == 10) {
+  } else if (warp == EW + 2) {
     if (lane == 0) {
       // ---------------- TMA producer: weight stages (one per chunk and tap)
       int aiss[AS];
@@ -1316,7 +1326,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
             if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
           }
     }
-  } else if (warp == 9) {
+  } else if (warp == EW + 1) {
     if (lane == 0) {
       // ---------------- MMA issuer: M = 128 channels, N = the tile's time rows (<= 256)
       // The tensor pipe queues few MMAs, so every instruction this thread spends between two
@@ -1385,8 +1395,9 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 0..7: lane quarter (channels) x time half
-    const int q = warp & 3, half = warp >> 2;
+    // ---------------- epilogue warps 0 .. EW-1: lane quarter (channels) x part of the time rows
+    const int q = warp & 3, part = warp >> 2;
+    constexpr int kParts = EW / 4;
     const uint32_t stg = stg0 + static_cast<uint32_t>(warp) * P::kStageWarp;
     int slot = 0;
     int it = 0;
@@ -1394,9 +1405,10 @@ __global__ void __launch_bounds__(kTNThreads, 1)
       const int ab = it & 1;
       const TNTile tile = tn_tile(g, t, mt, tt, ntiles);
       const int z = tile.z, mi = tile.mi, r0 = tile.r0;
-      // this warp's 32-row blocks of the tile: half 0 takes the first ceil(nblk / 2)
-      const int nblk = (tile.nr + 31) / 32, bh = (nblk + 1) / 2;
-      const int b0 = half * bh, nb = half ? nblk - bh : bh;
+      // this warp's 32-row blocks of the tile: part p takes blocks [p * bh, (p + 1) * bh)
+      const int nblk = (tile.nr + 31) / 32, bh = (nblk + kParts - 1) / kParts;
+      const int b0 = part * bh;
+      const int nb = b0 >= nblk ? 0 : (nblk - b0 < bh ? nblk - b0 : bh);
       const int te = r0 + tile.nr < g.m_rows ? r0 + tile.nr : g.m_rows;   // rows this tile stores
       const int co_row = mi * kBM + q * 32 + lane;
       const uint32_t tl = tmem + ab * kTNRows + (static_cast<uint32_t>(q * 32) << 16);
@@ -1464,7 +1476,7 @@ __global__ void __launch_bounds__(kTNThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == EW + 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
