@@ -911,18 +911,32 @@ constexpr int kTNRows = 256;    // time rows per tile (MMA N)
 #ifndef PTB_TN_A_STAGES
 #define PTB_TN_A_STAGES 4
 #endif
+// Residual-reading instances (two staged outputs, 4 KB of staging per warp) run 12 epilogue warps
+// and give up the third window slot for their staging: 5,040 -> 4,962 us per config-4 decode
+// (256-channel k3 convs2 82 -> 79 us, 128-channel k3 convs2 131 -> 121 us).  Three weight stages
+// instead of two window slots lose on the tensor-bound k7 / k11 convs2 layers (5,140).
+#ifndef PTB_RES_EW
+#define PTB_RES_EW 12
+#endif
+#ifndef PTB_RES_WS
+#define PTB_RES_WS 2
+#endif
+#ifndef PTB_RES_AS
+#define PTB_RES_AS PTB_TN_A_STAGES
+#endif
 template <int F>
 struct TNCfg {
-  static constexpr int kWinSlots = PTB_TN_WIN_SLOTS;
+  static constexpr bool kRes = F != EF_GENERIC && (F & EF_RES);
+  static constexpr int kWinSlots = kRes ? PTB_RES_WS : PTB_TN_WIN_SLOTS;
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
-  static constexpr int kAStages = PTB_TN_A_STAGES;
+  static constexpr int kAStages = kRes ? PTB_RES_AS : PTB_TN_A_STAGES;
   // Single-output instances without residual or branch-sum inputs (conv_pre, convs1, conv_post)
   // run 16 epilogue warps of one staging slot each: their epilogue is a chain of short dependent
   // steps per 16-row pass, and on the 128-channel k = 3 layers it, not the MMA, sets the pace;
   // twice the warps hide twice the latency in the same registers and shared memory.
-  static constexpr int kEpiWarps = (F == EF_OUT1 || F == EF_OUT0) ? 16 : 8;
+  static constexpr int kEpiWarps = (F == EF_OUT1 || F == EF_OUT0) ? 16 : kRes ? PTB_RES_EW : 8;
   static constexpr int kThreads = 32 * (kEpiWarps + 3);
   static constexpr int kSlots = kEpiWarps == 16 ? 1 : 2;          // staging slots per warp
   static constexpr int kStageWarp = kSlots * 16 * kBK * 4;        // slots x (16 rows x 32 channels)
