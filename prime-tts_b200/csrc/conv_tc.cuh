@@ -940,7 +940,7 @@ struct TNCfg {
   static constexpr int kThreads = 32 * (kEpiWarps + 3);
   static constexpr int kSlots = kEpiWarps == 16 ? 1 : 2;          // staging slots per warp
   static constexpr int kStageWarp = kSlots * 16 * kBK * 4;        // slots x (16 rows x 32 channels)
-  static constexpr int kStage = kEpiWarps * kStageWarp;           // 32 KiB output staging
+  static constexpr int kStage = kEpiWarps * kStageWarp;           // 32 KiB (48 KiB at 12 warps)
   static constexpr int kBytes = kWinSlots * kWinBytes + kAStages * kA + kStage + 1024 + 256;
   static_assert(kBytes <= 227 * 1024, "TN kernel shared memory over the per-CTA limit");
 };
