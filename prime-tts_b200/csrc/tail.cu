@@ -72,6 +72,27 @@ __device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, 
   iv = __fmul_rn(mag, sn);
 }
 
+// Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums in double, k ascending, zero basis
+// entries skipped, then the window; `out` is the frame row's band slice.
+template <int N0>
+__device__ __forceinline__ void basis_half(const double (&rv)[9], const double (&iv)[9], float *out) {
+  double er[8], ei[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0;
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    const double r = rv[k], i = iv[k];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const double bc = c_bcd[k * 16 + N0 + j], bs = c_bsd[k * 16 + N0 + j];
+      if (bc != 0.0) er[j] = __fma_rn(bc, r, er[j]);
+      if (bs != 0.0) ei[j] = __fma_rn(bs, i, ei[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) out[N0 + j] = __fmul_rn(__fadd_rn((float)er[j], (float)ei[j]), c_win[N0 + j]);
+}
+
 __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a) {
   extern __shared__ __align__(16) unsigned char tail_smem[];
   TailSmem &S = *reinterpret_cast<TailSmem *>(tail_smem);
@@ -105,33 +126,41 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   const long long F0 = ((m_lo + 8) >> 2) - 3;
   const int NF = (int)(((m_hi + 8) >> 2) - F0 + 1);
 
-  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im; two bins a thread at a time
-  // (independent chains in flight).  Frames outside [0, Tp) never reach the overlap-add: zeros.
-  for (int it = threadIdx.x; it < NF * 36; it += 2 * blockDim.x) {
-    const int it2 = it + blockDim.x;
-    const int fl = it / 36, rb = it - fl * 36, b = rb / 9, k = rb - b * 9;
-    const int fl2 = it2 / 36, rb2 = it2 - fl2 * 36, b2 = rb2 / 9, k2 = rb2 - b2 * 9;
-    const long long f = F0 + fl, f2 = F0 + fl2;
-    const bool v1 = f >= 0 && f < Tp, v2 = it2 < NF * 36 && f2 >= 0 && f2 < Tp;
-    float la = 0.0f, lb = 0.0f, la2 = 0.0f, lb2 = 0.0f;
-    if (v1) {
-      const float *pf = post + f * a.st_t;
-      la = pf[(long long)(b * 18 + k) * a.st_c];
-      lb = pf[(long long)(b * 18 + 9 + k) * a.st_c];
-    }
-    if (v2) {
-      const float *pf = post + f2 * a.st_t;
-      la2 = pf[(long long)(b2 * 18 + k2) * a.st_c];
-      lb2 = pf[(long long)(b2 * 18 + 9 + k2) * a.st_c];
-    }
-    float rv, iv, rv2, iv2;
-    tr_bin(la, lb, f32, rv, iv);
-    tr_bin(la2, lb2, f32, rv2, iv2);
-    re[fl][b][k] = v1 ? (double)rv : 0.0;
-    im[fl][b][k] = v1 ? (double)iv : 0.0;
-    if (it2 < NF * 36) {
-      re[fl2][b2][k2] = v2 ? (double)rv2 : 0.0;
-      im[fl2][b2][k2] = v2 ? (double)iv2 : 0.0;
+  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im.  Thread t < 252 owns bin
+  // t % 36 of frames t / 36, t / 36 + 7, ...: the bin's column, band and basis row are fixed per
+  // thread, so the loop carries only pointers; two frames at a time (independent chains in
+  // flight).  Frames outside [0, Tp) never reach the overlap-add: zeros.
+  static_assert(kTailThreads >= 252, "phase 1a maps 7 frames x 36 bins onto the threads");
+  if (threadIdx.x < 252) {
+    const int rb = threadIdx.x % 36, fl0 = threadIdx.x / 36, b = rb / 9, k = rb - b * 9;
+    const long long flo_l = -F0 > 0 ? -F0 : 0, fhi_l = Tp - F0 < NF ? Tp - F0 : NF;
+    const int flo = (int)flo_l, fhi = (int)fhi_l;   // valid frames [flo, fhi) of [0, NF)
+    const long long cst = a.st_c;
+    const float *pc = post + (long long)(b * 18 + k) * cst;
+    double *pre = &re[0][b][k], *pim = &im[0][b][k];
+    for (int fl = fl0; fl < NF; fl += 14) {
+      const int fl2 = fl + 7;
+      const bool v1 = fl >= flo && fl < fhi, v2 = fl2 < NF && fl2 >= flo && fl2 < fhi;
+      float la = 0.0f, lb = 0.0f, la2 = 0.0f, lb2 = 0.0f;
+      if (v1) {
+        const float *pf = pc + (F0 + fl) * a.st_t;
+        la = pf[0];
+        lb = pf[9 * cst];
+      }
+      if (v2) {
+        const float *pf = pc + (F0 + fl2) * a.st_t;
+        la2 = pf[0];
+        lb2 = pf[9 * cst];
+      }
+      float rv, iv, rv2, iv2;
+      tr_bin(la, lb, f32, rv, iv);
+      tr_bin(la2, lb2, f32, rv2, iv2);
+      pre[fl * 36] = v1 ? (double)rv : 0.0;
+      pim[fl * 36] = v1 ? (double)iv : 0.0;
+      if (fl2 < NF) {
+        pre[fl2 * 36] = v2 ? (double)rv2 : 0.0;
+        pim[fl2 * 36] = v2 ? (double)iv2 : 0.0;
+      }
     }
   }
   __syncthreads();
@@ -147,23 +176,11 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     for (int it = threadIdx.x; it < 2 * span; it += blockDim.x) {
       const int half = it >= span, fb = it - half * span;
       if (fb >= nfb) continue;
-      const int fl = fb >> 2, b = fb & 3, n0 = half * 8;
-      double er[8], ei[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0;
-#pragma unroll
-      for (int k = 0; k < 9; ++k) {
-        const double rv = re[fl][b][k], iv = im[fl][b][k];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const double bc = c_bcd[k * 16 + n0 + j], bs = c_bsd[k * 16 + n0 + j];
-          if (bc != 0.0) er[j] = __fma_rn(bc, rv, er[j]);
-          if (bs != 0.0) ei[j] = __fma_rn(bs, iv, ei[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        fr[fl][b * 16 + n0 + j] = __fmul_rn(__fadd_rn((float)er[j], (float)ei[j]), c_win[n0 + j]);
+      const int fl = fb >> 2, b = fb & 3;
+      // each half as its own code path: the basis offsets become compile-time constants, so the
+      // constants are instruction operands instead of one load each
+      if (half) basis_half<8>(re[fl][b], im[fl][b], &fr[fl][b * 16]);
+      else basis_half<0>(re[fl][b], im[fl][b], &fr[fl][b * 16]);
     }
   }
   __syncthreads();
