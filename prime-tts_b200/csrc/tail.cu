@@ -73,7 +73,10 @@ __device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, 
 }
 
 // Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums in double, k ascending, zero basis
-// entries skipped, then the window; `out` is the frame row's band slice.
+// entries skipped, then the window; `out` is the frame row's band slice.  The zero entries are
+// known in advance: the sine basis is exactly zero at k = 0 and at n = 0 (sin 0) and nowhere
+// else, the cosine basis nowhere (cos of a nonzero multiple of pi / 8 rounds to a nonzero float:
+// cos(pi / 2) in double is 6.1e-17); the host checks both when it builds the tables.
 template <int N0>
 __device__ __forceinline__ void basis_half(const double (&rv)[9], const double (&iv)[9], float *out) {
   double er[8], ei[8];
@@ -84,9 +87,8 @@ __device__ __forceinline__ void basis_half(const double (&rv)[9], const double (
     const double r = rv[k], i = iv[k];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const double bc = c_bcd[k * 16 + N0 + j], bs = c_bsd[k * 16 + N0 + j];
-      if (bc != 0.0) er[j] = __fma_rn(bc, r, er[j]);
-      if (bs != 0.0) ei[j] = __fma_rn(bs, i, ei[j]);
+      er[j] = __fma_rn(c_bcd[k * 16 + N0 + j], r, er[j]);
+      if (k != 0 && N0 + j != 0) ei[j] = __fma_rn(c_bsd[k * 16 + N0 + j], i, ei[j]);
     }
   }
 #pragma unroll
@@ -286,6 +288,9 @@ static void tail_constants_init() {
   for (int i = 0; i < 144; ++i) {
     bcd[i] = (double)bc[i];
     bsd[i] = (double)bs[i];
+    // the kernel skips exactly these zero entries (basis_half)
+    const int k = i / 16, n = i % 16;
+    if (bc[i] == 0.0f || (bs[i] == 0.0f) != (k == 0 || n == 0)) g_tail_err = 2;
   }
   if (cudaMemcpyToSymbol(c_bcd, bcd, sizeof(bcd)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_bsd, bsd, sizeof(bsd)) != cudaSuccess ||
@@ -307,6 +312,7 @@ static int tail_ready() {
   if (!done[dev]) {
     g_tail_err = 0;
     tail_constants_init();
+    PTB_REQUIRE(g_tail_err != 2, "pt_b200: iSTFT basis zeros differ from the kernel's assumption");
     PTB_REQUIRE(!g_tail_err, "pt_b200: tail constant upload failed");
     PTB_CUDA(cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sizeof(TailSmem)));
