@@ -21,7 +21,10 @@
 namespace ptb {
 
 constexpr int kTailW = 1024;                 // output samples per CTA (static smem < 48 KiB)
-constexpr int kTailThreads = 256;
+// 9 warps: 8 frames x 36 bins in the magnitude / phase phase, the 576 (frame, band, half) basis
+// items of a chunk in two rounds, the 276 staged overlap-add samples in one; the PQMF phase uses 8
+constexpr int kTailThreads = 288;
+constexpr int kTailP3 = 256;
 constexpr int kTailF = kTailW / 16 + 8;      // staged frames (chunk + halo): NF <= W/16 + 5
 constexpr int kTailM = kTailW / 4 + 20;      // staged trimmed-OLA samples per band
 
@@ -128,32 +131,37 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   const long long F0 = ((m_lo + 8) >> 2) - 3;
   const int NF = (int)(((m_hi + 8) >> 2) - F0 + 1);
 
-  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im.  Thread t < 252 owns bin
-  // t % 36 of frames t / 36, t / 36 + 7, ...: the bin's column, band and basis row are fixed per
+  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im.  Thread t owns bin t % 36 of
+  // frames t / 36, t / 36 + 8, ...: the bin's column, band and basis row are fixed per
   // thread, so the loop carries only pointers; two frames at a time (independent chains in
-  // flight).  Frames outside [0, Tp) never reach the overlap-add: zeros.
-  static_assert(kTailThreads >= 252, "phase 1a maps 7 frames x 36 bins onto the threads");
-  if (threadIdx.x < 252) {
+  // flight), the next two frames' loads issued before this pair's math.  Frames outside
+  // [0, Tp) never reach the overlap-add: zeros.
+  static_assert(kTailThreads == 288, "phase 1a maps 8 frames x 36 bins onto the threads");
+  {
     const int rb = threadIdx.x % 36, fl0 = threadIdx.x / 36, b = rb / 9, k = rb - b * 9;
     const long long flo_l = -F0 > 0 ? -F0 : 0, fhi_l = Tp - F0 < NF ? Tp - F0 : NF;
     const int flo = (int)flo_l, fhi = (int)fhi_l;   // valid frames [flo, fhi) of [0, NF)
     const long long cst = a.st_c;
     const float *pc = post + (long long)(b * 18 + k) * cst;
     double *pre = &re[0][b][k], *pim = &im[0][b][k];
-    for (int fl = fl0; fl < NF; fl += 14) {
-      const int fl2 = fl + 7;
+    auto ld = [&](int f, float &x, float &y) {
+      x = 0.0f;
+      y = 0.0f;
+      if (f < NF && f >= flo && f < fhi) {
+        const float *pf = pc + (F0 + f) * a.st_t;
+        x = pf[0];
+        y = pf[9 * cst];
+      }
+    };
+    float na, nb, na2, nb2;
+    ld(fl0, na, nb);
+    ld(fl0 + 8, na2, nb2);
+    for (int fl = fl0; fl < NF; fl += 16) {
+      const int fl2 = fl + 8;
       const bool v1 = fl >= flo && fl < fhi, v2 = fl2 < NF && fl2 >= flo && fl2 < fhi;
-      float la = 0.0f, lb = 0.0f, la2 = 0.0f, lb2 = 0.0f;
-      if (v1) {
-        const float *pf = pc + (F0 + fl) * a.st_t;
-        la = pf[0];
-        lb = pf[9 * cst];
-      }
-      if (v2) {
-        const float *pf = pc + (F0 + fl2) * a.st_t;
-        la2 = pf[0];
-        lb2 = pf[9 * cst];
-      }
+      const float la = na, lb = nb, la2 = na2, lb2 = nb2;
+      ld(fl + 16, na, nb);          // next pair's loads in flight during this pair's math
+      ld(fl + 24, na2, nb2);
       float rv, iv, rv2, iv2;
       tr_bin(la, lb, f32, rv, iv);
       tr_bin(la2, lb2, f32, rv2, iv2);
@@ -226,7 +234,8 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   float *wav = a.wav + (a.wav0 ? a.wav0[req] : 0);
   const int jn = (int)(nwav - j0 < kTailW ? nwav - j0 : kTailW);
   const int klo = (int)keep_lo, khi = (int)(keep_hi < nwav ? keep_hi : nwav);
-  static_assert(kTailW == 16 * kTailThreads / 4, "phase 3 gives every thread four outputs");
+  static_assert(kTailW == 16 * kTailP3 / 4, "phase 3 gives each of its threads four outputs");
+  if (threadIdx.x >= kTailP3) return;
   const int p = threadIdx.x & 3, g = threadIdx.x >> 2;
   const int k0 = (31 - p) & 3, ntap = (63 - k0 + 3) >> 2;
   // j0 is a multiple of 4, so j + k0 - 31 is: the shift divides exactly
