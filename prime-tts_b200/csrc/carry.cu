@@ -222,7 +222,7 @@ int run_pass(pt_b200_carry *c, cudaStream_t st, int k, const float *z_dev, float
     return run_conv(d, st, W, act, rows, off0, step, e, c->tiles + off, cnt);
   };
   if (P.zchunks[k] > 0) {
-    dim3 grid((unsigned)P.zchunks[k], 192 / 32, (unsigned)n);
+    dim3 grid((unsigned)P.zchunks[k], 1, (unsigned)n);
     stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.zld, c->f1 + o, p.a0, c->f0 + o, c->Z);
     PTB_CUDA(cudaGetLastError());
     count_launch();

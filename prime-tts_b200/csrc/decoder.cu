@@ -54,27 +54,31 @@ int make_layer(DLayer *L, const float *wp, const float *bias, int rows4, int nta
 }  // namespace
 
 // scatter each request's channel-major latent columns (z[zoff + c*zld + t], f0 <= t < T) into the
-// level-0 rows, tf32-rounded
+// level-0 rows, tf32-rounded.  One 32 x 8 block moves 32 frames x all 192 channels: every thread
+// issues its 24 loads before the barrier, and each frame row leaves as six 128-byte lines.
 __global__ void ptb::dec::stage_z_kernel(const float *__restrict__ z, const long long *__restrict__ zoff,
                                const long long *__restrict__ zld, const long long *__restrict__ T,
                                const long long *__restrict__ a0, const long long *__restrict__ f0,
                                float *__restrict__ Z) {
-  __shared__ float tile[32][33];
+  __shared__ float tile[192][33];
   const int r = blockIdx.z;
   const long long Tr = T[r];   // frames [f0, T) of request r (f0 null: from 0)
   const long long t0 = (f0 ? f0[r] : 0) + (long long)blockIdx.x * 32;
   if (t0 >= Tr) return;
-  const int c0 = blockIdx.y * 32;
   const float *zr = z + zoff[r];
   const long long ld = zld[r];
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const long long t = t0 + threadIdx.x;
-    tile[i][threadIdx.x] = t < Tr ? zr[(long long)(c0 + i) * ld + t] : 0.0f;
-  }
+  const long long t = t0 + threadIdx.x;
+  const bool tv = t < Tr;
+#pragma unroll 8
+  for (int c = threadIdx.y; c < 192; c += 8) tile[c][threadIdx.x] = tv ? zr[(long long)c * ld + t] : 0.0f;
   __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const long long t = t0 + i;
-    if (t < Tr) Z[(a0[r] + t) * 192 + c0 + threadIdx.x] = tf32_rna(tile[threadIdx.x][i]);
+  const long long a = a0[r];
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const long long tt = t0 + i;
+    if (tt >= Tr) break;
+    float *dst = Z + (a + tt) * 192;
+#pragma unroll
+    for (int c = threadIdx.x; c < 192; c += 32) dst[c] = tf32_rna(tile[c][i]);
   }
 }
 
@@ -323,7 +327,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   // latents -> level-0 rows
   rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
-    dim3 grid((unsigned)((p.max_T + 31) / 32), 192 / 32, (unsigned)nreq);
+    dim3 grid((unsigned)((p.max_T + 31) / 32), 1, (unsigned)nreq);
     stage_z_kernel<<<grid, dim3(32, 8), 0, st>>>(z_dev, p.zoff, p.zld, p.Td, p.a0, nullptr, d->Z);
     PTB_CUDA(cudaGetLastError());
     count_launch();
