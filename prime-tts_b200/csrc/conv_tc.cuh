@@ -208,10 +208,10 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &e, const float (
         v[i + 2] = a4.z + v[i + 2];
         v[i + 3] = a4.w + v[i + 3];
       } else {
-        v[i + 0] = (a4.x + v[i + 0]) / 3.0f;
-        v[i + 1] = (a4.y + v[i + 1]) / 3.0f;
-        v[i + 2] = (a4.z + v[i + 2]) / 3.0f;
-        v[i + 3] = (a4.w + v[i + 3]) / 3.0f;
+        v[i + 0] = div3_rn(a4.x + v[i + 0]);
+        v[i + 1] = div3_rn(a4.y + v[i + 1]);
+        v[i + 2] = div3_rn(a4.z + v[i + 2]);
+        v[i + 3] = div3_rn(a4.w + v[i + 3]);
       }
     }
   }
@@ -604,7 +604,7 @@ __device__ __forceinline__ void rows_chunk(const EpiParams &e, float (&v)[32], l
     for (int i = 0; i < 32; ++i) v[i] = ac[i] + v[i];
   } else if (e.acc_mode == 3) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = (ac[i] + v[i]) / 3.0f;
+    for (int i = 0; i < 32; ++i) v[i] = div3_rn(ac[i] + v[i]);
   }
   const long long off = orow * e.ldc + col0;
   if (e.out0) {
@@ -1118,7 +1118,7 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
         float x = v[i] + bias;
         if (hr) x += rs[i];
         if (am == 2) x = ac[i] + x;
-        else if (am == 3) x = (ac[i] + x) / 3.0f;
+        else if (am == 3) x = div3_rn(ac[i] + x);
         wv[i] = tf32_rna(leaky(x, e.alpha1));
       }
 #pragma unroll
@@ -1137,7 +1137,7 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
         float x = v[i] + bias;
         if (hr) x += rs[i];
         if (am == 2) x = ac[i] + x;
-        else if (am == 3) x = (ac[i] + x) / 3.0f;
+        else if (am == 3) x = div3_rn(ac[i] + x);
         const uint32_t at = static_cast<uint32_t>(i * kBK * 4 + lane * 4);
         if (o0) st_shared_f32(s0 + at, ok ? x : 0.0f);
         if (o1) st_shared_f32(s1 + at, ok ? tf32_rna(leaky(x, e.alpha1)) : 0.0f);
@@ -1197,7 +1197,7 @@ __device__ __forceinline__ void tn_rows_pass(const EpiParams &e, uint32_t taddr,
     if constexpr (MODE == EPI_ROWS) {
       if (hr) x += rs[i];
       if (am == 2) x = ac[i] + x;
-      else if (am == 3) x = (ac[i] + x) / 3.0f;
+      else if (am == 3) x = div3_rn(ac[i] + x);
     }
     if (o0) e.out0[orow * ldc + col] = x;
     if (o1) {

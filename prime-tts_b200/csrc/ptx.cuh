@@ -217,6 +217,18 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// x / 3 correctly rounded (what IEEE division gives) without the division routine: q = RN(x * r)
+// with r = RN(1/3), then one correction step with the exact residual x - 3q (an FMA computes it
+// exactly): the correction method for division by a constant (Markstein's quotient refinement).
+// Checked against IEEE x / 3 for every finite fp32 x; the only difference, x = -0, is returned as
+// q itself (an exact quotient needs no correction), and so is +-Inf (whose residual is NaN).
+__device__ __forceinline__ float div3_rn(float x) {
+  const float r = 0.3333333432674407958984375f;   // RN(1/3)
+  const float q = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q, 3.0f, x);
+  return (e == 0.0f || isinf(x)) ? q : __fmaf_rn(e, r, q);
+}
+
 // fp32 -> tf32 with round-to-nearest (ties away), the value kept in an fp32 container.
 // Integer form: add half of the 13 dropped mantissa bits to the magnitude and truncate (ties go
 // away from zero; a mantissa carry moves into the exponent).  Inf and NaN pass unchanged.  It is
