@@ -55,15 +55,22 @@ struct TailArgs {
   float *wav;
 };
 
-__device__ __forceinline__ float tr_exp(float x, bool f32) { return f32 ? expf(x) : (float)exp((double)x); }
-__device__ __forceinline__ float tr_sin(float x, bool f32) { return f32 ? sinf(x) : (float)sin((double)x); }
 // magnitude / phase of one bin: re = exp(a) * cos(pi * sin(b)), im = exp(a) * sin(pi * sin(b))
-// (the cosine and sine of the phase come from one sincos call: one argument reduction)
-__device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, float &iv) {
-  const float mag = tr_exp(la, f32);
-  const float ph = __fmul_rn(tr_sin(lb, f32), 3.1415927410125732f);
-  float c, sn;
-  if (f32) {
+// (the cosine and sine of the phase come from one sincos call: one argument reduction).  F32:
+// the fp32 functions; otherwise double-precision ones rounded to fp32 (the reference's choice
+// for small tensors).
+template <bool F32>
+__device__ __forceinline__ void tr_bin(float la, float lb, float &rv, float &iv) {
+  float mag, sb, c, sn;
+  if constexpr (F32) {
+    mag = expf(la);
+    sb = sinf(lb);
+  } else {
+    mag = (float)exp((double)la);
+    sb = (float)sin((double)lb);
+  }
+  const float ph = __fmul_rn(sb, 3.1415927410125732f);
+  if constexpr (F32) {
     sincosf(ph, &sn, &c);
   } else {
     double sd, cd;
@@ -73,6 +80,42 @@ __device__ __forceinline__ void tr_bin(float la, float lb, bool f32, float &rv, 
   }
   rv = __fmul_rn(mag, c);
   iv = __fmul_rn(mag, sn);
+}
+
+// Phase 1a loop of one thread: its bin's frames fl0, fl0 + 8, ... of [0, NF), two at a time, the
+// next two frames' loads issued before this pair's math; frames outside [flo, fhi) are zeros.
+template <bool F32>
+__device__ __forceinline__ void bins_loop(const float *pc, long long st_t, long long cst,
+                                          long long F0, int NF, int flo, int fhi, int fl0,
+                                          double *pre, double *pim) {
+  auto ld = [&](int f, float &x, float &y) {
+    x = 0.0f;
+    y = 0.0f;
+    if (f < NF && f >= flo && f < fhi) {
+      const float *pf = pc + (F0 + f) * st_t;
+      x = pf[0];
+      y = pf[9 * cst];
+    }
+  };
+  float na, nb, na2, nb2;
+  ld(fl0, na, nb);
+  ld(fl0 + 8, na2, nb2);
+  for (int fl = fl0; fl < NF; fl += 16) {
+    const int fl2 = fl + 8;
+    const bool v1 = fl >= flo && fl < fhi, v2 = fl2 < NF && fl2 >= flo && fl2 < fhi;
+    const float la = na, lb = nb, la2 = na2, lb2 = nb2;
+    ld(fl + 16, na, nb);
+    ld(fl + 24, na2, nb2);
+    float rv, iv, rv2, iv2;
+    tr_bin<F32>(la, lb, rv, iv);
+    tr_bin<F32>(la2, lb2, rv2, iv2);
+    pre[fl * 36] = v1 ? (double)rv : 0.0;
+    pim[fl * 36] = v1 ? (double)iv : 0.0;
+    if (fl2 < NF) {
+      pre[fl2 * 36] = v2 ? (double)rv2 : 0.0;
+      pim[fl2 * 36] = v2 ? (double)iv2 : 0.0;
+    }
+  }
 }
 
 // Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums in double, k ascending, zero basis
@@ -144,34 +187,9 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     const long long cst = a.st_c;
     const float *pc = post + (long long)(b * 18 + k) * cst;
     double *pre = &re[0][b][k], *pim = &im[0][b][k];
-    auto ld = [&](int f, float &x, float &y) {
-      x = 0.0f;
-      y = 0.0f;
-      if (f < NF && f >= flo && f < fhi) {
-        const float *pf = pc + (F0 + f) * a.st_t;
-        x = pf[0];
-        y = pf[9 * cst];
-      }
-    };
-    float na, nb, na2, nb2;
-    ld(fl0, na, nb);
-    ld(fl0 + 8, na2, nb2);
-    for (int fl = fl0; fl < NF; fl += 16) {
-      const int fl2 = fl + 8;
-      const bool v1 = fl >= flo && fl < fhi, v2 = fl2 < NF && fl2 >= flo && fl2 < fhi;
-      const float la = na, lb = nb, la2 = na2, lb2 = nb2;
-      ld(fl + 16, na, nb);          // next pair's loads in flight during this pair's math
-      ld(fl + 24, na2, nb2);
-      float rv, iv, rv2, iv2;
-      tr_bin(la, lb, f32, rv, iv);
-      tr_bin(la2, lb2, f32, rv2, iv2);
-      pre[fl * 36] = v1 ? (double)rv : 0.0;
-      pim[fl * 36] = v1 ? (double)iv : 0.0;
-      if (fl2 < NF) {
-        pre[fl2 * 36] = v2 ? (double)rv2 : 0.0;
-        pim[fl2 * 36] = v2 ? (double)iv2 : 0.0;
-      }
-    }
+    // the fp32 / double choice is per request: one code path per CTA, not a branch per bin
+    if (f32) bins_loop<true>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
+    else bins_loop<false>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
   }
   __syncthreads();
   // ---- 1b. per (frame, band, half of the 16 output bins): the 9 -> 16 basis sums in double,
