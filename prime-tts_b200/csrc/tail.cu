@@ -20,7 +20,7 @@
 
 namespace ptb {
 
-constexpr int kTailW = 1024;                 // output samples per CTA (static smem < 48 KiB)
+constexpr int kTailW = 1024;                 // output samples per CTA (66.5 KB of shared memory)
 // 9 warps: 8 frames x 36 bins in the magnitude / phase phase, the 576 (frame, band, half) basis
 // items of a chunk in two rounds, the 276 staged overlap-add samples in one; the PQMF phase uses 8
 constexpr int kTailThreads = 288;
@@ -28,8 +28,8 @@ constexpr int kTailP3 = 256;
 constexpr int kTailF = kTailW / 16 + 8;      // staged frames (chunk + halo): NF <= W/16 + 5
 constexpr int kTailM = kTailW / 4 + 20;      // staged trimmed-OLA samples per band
 
-__constant__ float c_bc[144], c_bs[144], c_win[16], c_win2[16];
-__constant__ double c_bcd[144], c_bsd[144];   // the same bases, exact in double
+__constant__ float c_win[16], c_win2[16];
+__constant__ double c_bcd[144], c_bsd[144];   // the fp32 basis values, held exactly in double
 
 // Frame rows are 68 floats (4 bands x 16 + 4 pad): the overlap-add reads 8 consecutive frames at
 // one (band, sample) per warp and the stride of 68 puts those reads on 32 distinct banks.
@@ -321,8 +321,6 @@ static void tail_constants_init() {
   }
   if (cudaMemcpyToSymbol(c_bcd, bcd, sizeof(bcd)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_bsd, bsd, sizeof(bsd)) != cudaSuccess ||
-      cudaMemcpyToSymbol(c_bc, bc, sizeof(bc)) != cudaSuccess ||
-      cudaMemcpyToSymbol(c_bs, bs, sizeof(bs)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win, win, sizeof(win)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win2, win2, sizeof(win2)) != cudaSuccess)
     g_tail_err = 1;
