@@ -29,6 +29,8 @@
 // than stage j+1's convs2 has already overwritten it.  The planner checks these orders.
 #include <algorithm>
 
+#include <vector>
+
 #include "decoder.cuh"
 
 using namespace ptb;
@@ -202,6 +204,18 @@ struct pt_b200_carry {
   float *U[2], *LU[2], *ACC[2], *OUT[2], *H[2][3], *XB[2][3], *XT[2][3][2];
   int2 *tiles = nullptr;
   long long *f0 = nullptr, *f1 = nullptr, *klo = nullptr, *khi = nullptr, *jb = nullptr;
+  // One CUDA graph per pass: a pass's launches depend only on the session's plan and on the
+  // latent / waveform buffers and stream it ran with, so the second identical run of a pass
+  // captures it and later runs replay it (PT_B200_GRAPH=0: always eager).
+  struct PassGraph {
+    cudaGraphExec_t exec = nullptr;
+    const float *z = nullptr;
+    float *wav = nullptr;
+    cudaStream_t st = nullptr;
+    bool seen = false;
+    long kernels = 0;
+  };
+  std::vector<PassGraph> graphs;
 };
 
 namespace {
@@ -411,7 +425,43 @@ int pt_b200_carry_run(pt_b200_carry *c, void *stream, int pass, const float *z_d
   std::lock_guard<std::mutex> lk(d->mu);
   PTB_CUDA(cudaSetDevice(d->device));
   cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
-  if (run_pass(c, st, pass, z_dev, wav_dev)) return -1;
+  if (d->graph_on < 0) d->graph_on = getenv("PT_B200_GRAPH") ? atoi(getenv("PT_B200_GRAPH")) : 1;
+  if (c->graphs.size() != (size_t)c->P.npass) c->graphs.assign((size_t)c->P.npass, {});
+  pt_b200_carry::PassGraph &G = c->graphs[(size_t)pass];
+  const bool same = G.z == z_dev && G.wav == wav_dev && G.st == st;
+  if (!d->graph_on || !same || !G.seen) {
+    // first run with these buffers: eager (one-time uploads and attribute settings happen here)
+    if (G.exec && !same) {
+      cudaGraphExecDestroy(G.exec);
+      G.exec = nullptr;
+    }
+    G.z = z_dev;
+    G.wav = wav_dev;
+    G.st = st;
+    G.seen = true;
+    if (run_pass(c, st, pass, z_dev, wav_dev)) return -1;
+  } else {
+    if (!G.exec) {
+      const long before = launches(0);
+      PTB_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      const int rc = run_pass(c, st, pass, z_dev, wav_dev);
+      cudaGraph_t g = nullptr;
+      const cudaError_t ec = cudaStreamEndCapture(st, &g);
+      const long captured = launches(0) - before;
+      count_launch(-captured);   // capturing launches nothing
+      if (rc || ec != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        PTB_REQUIRE(false, "pt_b200: carried pass %d graph capture failed (%s)", pass,
+                    cudaGetErrorString(ec));
+      }
+      const cudaError_t ei = cudaGraphInstantiate(&G.exec, g, 0);
+      cudaGraphDestroy(g);
+      PTB_CUDA(ei);
+      G.kernels = captured;
+    }
+    PTB_CUDA(cudaGraphLaunch(G.exec, st));
+    count_launch(G.kernels);
+  }
   ++c->next;
   return 0;
 }
@@ -429,6 +479,8 @@ void pt_b200_carry_close(pt_b200_carry *c) {
     cudaSetDevice(c->d->device);
     cudaDeviceSynchronize();
   }
+  for (auto &G : c->graphs)
+    if (G.exec) cudaGraphExecDestroy(G.exec);
   if (c->block) cudaFree(c->block);
   if (c->lay.table_block) cudaFree(c->lay.table_block);
   delete c;

@@ -174,3 +174,28 @@ def test_config5_carried(dec):
     dec.sync(s.cuda_stream)
     dec.stream_carry_device(Ta, z.data_ptr(), got.data_ptr(), 32, s.cuda_stream)
     assert torch.equal(got, full)
+
+
+def test_carried_session_rerun_replays_its_passes(dec):
+    """A session run again on the same buffers and stream replays each pass as a captured CUDA
+    graph (the first run is eager, the second captures): every run, and a run on another output
+    buffer, writes the whole decode's bits."""
+    import torch
+    Ts, chunk = [3, 70, 129, 40], 32
+    zs = _zs(Ts, 26)
+    full = torch.from_numpy(np.concatenate(dec.decode(zs)))
+    dev = torch.device("cuda", 0)
+    z = torch.from_numpy(np.concatenate([a.ravel() for a in zs])).to(dev)
+    wav = torch.empty(256 * sum(Ts), device=dev)
+    other = torch.empty_like(wav)
+    s = torch.cuda.Stream(device=dev)
+    sess = pt_b200.CarrySession(dec, Ts, chunk)
+    try:
+        for out in (wav, wav, wav, other, wav):
+            out.fill_(float("nan"))
+            torch.cuda.synchronize()
+            sess.run_all(z.data_ptr(), out.data_ptr(), s.cuda_stream)
+            dec.sync(s.cuda_stream)
+            assert torch.equal(out.cpu(), full)
+    finally:
+        sess.close()
