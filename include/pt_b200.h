@@ -265,6 +265,27 @@ PT_B200_API int pt_b200_decoder_profile(pt_b200_decoder *d, int enable);
 PT_B200_API int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double *ms,
                                              double *flops, double *bytes, int *kind);
 
+/* Per-layer checkpoints of one request, for parity against a CPU decode node by node (the
+ * batched decoder's counterpart of the reference's pt_v21_checkpoints, runtime/v21/src/
+ * pt_v21.h:204-206, which dumps graph-node outputs for the per-node gate of
+ * tests/v21_reference.py:430-447).  Decodes z_host [192][T] (host) on the decoder's stream,
+ * eagerly, and after each of the 40 conv launches copies that launch's output, without gap rows,
+ * channel-major, into ckpt[i] (host; NULL entries are skipped); wav_host [256*T] receives the
+ * waveform.  Layer i and the tensor it holds (L1 = 4T, L2 = 16T rows):
+ *   0  conv_pre + LeakyRelu                 [512][T]     (TF32-rounded, as the next conv reads it)
+ *   1  ups.0                                [256][L1]    (fp32)
+ *   2 + 6*rb + 2*j      convs1.j of resblock rb + LeakyRelu   [256][L1] (TF32-rounded)
+ *   3 + 6*rb + 2*j      convs2.j + residual: j < 2 the running x; j = 2: rb 0 the branch, rb 1
+ *                       the branch sum, rb 2 LeakyRelu((sum)/3)  [256][L1] (fp32; the last TF32)
+ *   20 ups.1                                [128][L2]
+ *   21 .. 38 as 2 .. 19 for resblocks 3..5 at 128 channels; 38 is LeakyRelu_0.01((sum)/3) with
+ *                       the reflection-pad row in front: [128][L2 + 1]
+ *   39 subband_conv_post                    [72][L2 + 1]
+ * A debugging entry point: it allocates its own device buffer and synchronises. */
+#define PT_B200_NCKPT 40
+PT_B200_API int pt_b200_decoder_checkpoints(pt_b200_decoder *d, const float *z_host, int64_t T,
+                                            float *const *ckpt, float *wav_host);
+
 /* One request, the reference's driver shape (an extension the survey lists as pt_v21_decode):
  * z [192][T] host -> wav [256*T] host. */
 PT_B200_API int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav);
@@ -374,10 +395,12 @@ PT_B200_API pt_b200_decoder *pt_b200_decoder_create_from_ptk(int device, const c
  * [cout4/4][K][cin][4], bias [cout] or NULL.  Scratch (staged input, re-laid-out weights) comes
  * from one fixed 16 MiB array inside the library on each device: calls needing more (T *
  * round_up(cin,32) + round_up(cout,16) * K * round_up(cin,32) floats, plus padding) are rejected
- * with -1 and a message.  The first call on a device looks up that array's device address, so
- * make it before any stream capture.  All calls on a device share the array: calls that overlap
- * on the GPU (other streams, other threads) race and must be serialised by the caller.  The call
- * returns after its work on `stream` (NULL = the default stream) has finished. */
+ * with -1 and a message, before any device work.  The first call on a device looks up that
+ * array's device address, so make it before any stream capture.  All calls on a device share the
+ * array: calls that overlap on the GPU (other streams, other threads) race and must be serialised
+ * by the caller.  The call is synchronous: it reads a device error word back into host memory
+ * and waits (with the library's bounded wait, PT_B200_WAIT_S) for its work on `stream`
+ * (NULL = the default stream) to finish before it returns. */
 PT_B200_API int pt_b200_conv_noalloc(int device, void *stream, const float *x, int64_t ldx,
                                      int64_t cin, int64_t T, float *y, int cout, int K, int pad,
                                      int dil, const float *wp, const float *bias, int epi0,

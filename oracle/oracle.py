@@ -127,6 +127,33 @@ class CpuDecoder:
         """weights: prime-tts_b200 ``DecoderWeights`` (packed numpy arrays); z [192][T]."""
         z = np.ascontiguousarray(z, np.float32)
         T = z.shape[-1]
+        wav = np.empty(256 * T, np.float32)
+        dw = self._weights(weights)
+        r = self._decode(C.byref(dw), _p(z), T, _p(wav))
+        if r != 0:
+            raise RuntimeError(f"{self.kind} decode failed ({r})")
+        return wav
+
+    def decode_checkpoints(self, weights, z: np.ndarray):
+        """The oracle's decode with the output of each of its 40 conv nodes (or_decode_ckpt; the
+        layer order and shapes of pt_b200_decoder_checkpoints): (list of 40 arrays, wav)."""
+        if self.kind != "oracle":
+            raise ValueError("checkpoints come from the restatement (kind='oracle')")
+        z = np.ascontiguousarray(z, np.float32)
+        T = z.shape[-1]
+        ck = [np.empty(s, np.float32) for s in checkpoint_shapes(T)]
+        arr = (_f * 40)(*[_p(a) for a in ck])
+        fn = self.lib.or_decode_ckpt
+        fn.argtypes = [C.POINTER(_DecW), _f, _i64, _f, C.POINTER(_f)]
+        fn.restype = C.c_int
+        wav = np.empty(256 * T, np.float32)
+        dw = self._weights(weights)
+        if fn(C.byref(dw), _p(z), T, _p(wav), arr) != 0:
+            raise RuntimeError("oracle checkpoint decode failed")
+        return ck, wav
+
+    @staticmethod
+    def _weights(weights):
         dw = _DecW()
         dw.pre_w, dw.pre_b = _p(weights.pre_w), _p(weights.pre_b)
         for i in range(2):
@@ -139,11 +166,29 @@ class CpuDecoder:
                 dw.rb_b2[r][j] = _p(weights.rb_b2[r][j])
         dw.post_w, dw.post_b = _p(weights.post_w), _p(weights.post_b)
         dw.pqmf = _p(weights.pqmf)
-        wav = np.empty(256 * T, np.float32)
-        r = self._decode(C.byref(dw), _p(z), T, _p(wav))
-        if r != 0:
-            raise RuntimeError(f"{self.kind} decode failed ({r})")
-        return wav
+        return dw
+
+
+def checkpoint_shapes(T: int) -> list:
+    """Shapes of the 40 per-layer checkpoints of a T-frame decode (conv launch order)."""
+    out = [(512, T)]
+    for s, (C_, L) in enumerate(((256, 4 * T), (128, 16 * T))):
+        out += [(C_, L)] * 19
+    out[38] = (128, 16 * T + 1)
+    out.append((72, 16 * T + 1))
+    return out
+
+
+def checkpoint_names() -> list:
+    """Names of the 40 checkpoints (graph layer names)."""
+    names = ["conv_pre"]
+    for s in range(2):
+        names.append(f"ups.{s}")
+        for rb in range(3):
+            for j in range(3):
+                names += [f"rb{3 * s + rb}.convs1.{j}", f"rb{3 * s + rb}.convs2.{j}"]
+    names.append("conv_post")
+    return names
 
 
 def overlap_save_windows(T: int, win: int, ctx: int, hop: int = 256) -> list:

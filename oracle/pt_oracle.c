@@ -339,7 +339,15 @@ static int conv_node(const float *x, int64_t T, int cin, int cout, int K, int pa
 /* Decoder wiring: ref/v21_graph_trace.txt nodes 3819-4065 with the interpreter's epilogue fusion
  * (a LeakyRelu whose input has that single consumer folds into the conv, pt_v21_host.c:3290-3333;
  * bit-identical to running it separately). */
+#define CK(i, src, count) \
+  do { if (ck && ck[i]) memcpy(ck[i], (src), sizeof(float) * (size_t) (count)); } while (0)
+
 int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
+  return or_decode_ckpt(w, z, T, wav, NULL);
+}
+
+int or_decode_ckpt(const or_dec_weights *w, const float *z, int64_t T, float *wav,
+                   float *const *ck) {
   static const int kk[3] = {3, 7, 11}, dd[3] = {1, 3, 5};
   const float lr = 0.10000000149011612f, lr_final = 0.009999999776482582f;
   int64_t L = T;
@@ -347,6 +355,7 @@ int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
   if (!x) return -1;
   /* conv_pre + LeakyRelu (node 3819/3820) */
   if (conv_node(z, T, 192, 512, 7, 3, 1, w->pre_w, w->pre_b, 1, lr, x)) return -1;
+  CK(0, x, 512 * T);
   int C = 512;
   for (int stage = 0; stage < 2; stage++) {
     const int Co = C / 2;
@@ -361,6 +370,7 @@ int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
     or_convT(x, L, C, L, u, Lo, Co, 4, 6, 16, w->ups_w[stage], w->ups_b[stage], 1);
     leaky(u, lu, (int64_t) Co * Lo, lr);
     const int64_t n = (int64_t) Co * Lo;
+    CK(1 + 19 * stage, u, n);
     for (int rb = 0; rb < 3; rb++) {
       const int r = stage * 3 + rb, K = kk[rb];
       memcpy(xr, u, sizeof(float) * n);          /* the running residual x starts at ups out */
@@ -370,15 +380,18 @@ int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
         if (conv_node(in, Lo, Co, Co, K, dd[j] * (K - 1) / 2, dd[j], w->rb_w1[r][j], w->rb_b1[r][j],
                       1, lr, h))
           return -1;
+        CK(2 + 19 * stage + 6 * rb + 2 * j, h, n);
         /* convs2.j (dilation 1) */
         if (conv_node(h, Lo, Co, Co, K, (K - 1) / 2, 1, w->rb_w2[r][j], w->rb_b2[r][j], 0, 0.0f, y))
           return -1;
         for (int64_t i = 0; i < n; i++) xr[i] = y[i] + xr[i];   /* resblocks.r/Add_j */
         if (j < 2) leaky(xr, xt, n, lr);                          /* LeakyRelu_(2j+2) */
+        if (j < 2) CK(3 + 19 * stage + 6 * rb + 2 * j, xr, n);
       }
       /* /dec/Add, /dec/Add_1: ((rb0 + rb1) + rb2) */
       if (rb == 0) memcpy(acc, xr, sizeof(float) * n);
       else for (int64_t i = 0; i < n; i++) acc[i] = acc[i] + xr[i];
+      if (rb < 2) CK(7 + 19 * stage + 6 * rb, acc, n);
     }
     free(x);
     x = malloc(sizeof(float) * n);
@@ -386,6 +399,7 @@ int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
     /* Div by 3 (node 3868/3917), then LeakyRelu 0.1 (3869) or 0.01 (3918) */
     for (int64_t i = 0; i < n; i++) acc[i] = acc[i] / 3.0f;
     leaky(acc, x, n, stage == 0 ? lr : lr_final);
+    if (stage == 0) CK(19, x, n);
     free(u); free(lu); free(xr); free(xt); free(h); free(y); free(acc);
     C = Co;
     L = Lo;
@@ -398,8 +412,10 @@ int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav) {
     xp[c * Tp] = x[c * L + 1];
     memcpy(xp + c * Tp + 1, x + c * L, sizeof(float) * L);
   }
+  CK(38, xp, 128 * Tp);
   /* subband_conv_post 128 -> 72 k7 p3 (node 3935; its consumer is a Reshape: no epilogue) */
   if (conv_node(xp, Tp, 128, 72, 7, 3, 1, w->post_w, w->post_b, 0, 0.0f, post)) return -1;
+  CK(39, post, 72 * Tp);
   const int r = or_tail(post, Tp, w->pqmf, wav);
   free(x); free(xp); free(post);
   return r;

@@ -58,6 +58,15 @@ typedef struct {
  * Graph wiring: ref/v21_graph_trace.txt nodes 3819-4065. */
 int or_decode(const or_dec_weights *w, const float *z, int64_t T, float *wav);
 
+/* The same decode, also copying the output of every conv node (with its fused epilogue, residual
+ * add, branch sum, /3 and LeakyRelu as the graph applies them) into ck[i] when ck and ck[i] are
+ * non-NULL.  The 40 layers and their shapes are those of pt_b200_decoder_checkpoints
+ * (include/pt_b200.h): 0 conv_pre+leaky [512][T]; 1 ups.0 [256][4T]; 2+6rb+2j convs1.j+leaky;
+ * 3+6rb+2j convs2.j + residual (j = 2: branch, branch sum, leaky(sum/3)); 20..38 the same at 128
+ * channels and 16T (38: the reflection-padded [128][16T+1]); 39 conv_post [72][16T+1]. */
+int or_decode_ckpt(const or_dec_weights *w, const float *z, int64_t T, float *wav,
+                   float *const *ck);
+
 /* The iSTFT + PQMF tail alone: post [72][Tp] (Tp = 16T+1 frames) -> wav [256T] with
  * 256T = 16 * 4 * (Tp - 1). Graph nodes 3957-4065. */
 int or_tail(const float *post, int64_t Tp, const float *pqmf, float *wav);

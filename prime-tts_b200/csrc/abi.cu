@@ -72,9 +72,11 @@ double wait_limit_s() {
   return v;
 }
 
+}  // namespace
+
 // Poll the stream with a deadline (the reference's pt_wait, runtime/v21/src/pt_v21_cuda.cu:30-57,
 // plus a limit): a stream that does not finish in time is reported, not waited on forever.
-int wait_stream(cudaStream_t s) {
+int ptb::wait_stream(cudaStream_t s) {
   const double t0 = now_s(), lim = wait_limit_s();
   for (unsigned it = 0;; ++it) {
     const cudaError_t e = cudaStreamQuery(s);
@@ -90,6 +92,8 @@ int wait_stream(cudaStream_t s) {
     sched_yield();
   }
 }
+
+namespace {
 
 // After a sync: report kernel-side errors (bounded waits that gave up, rejected arguments).
 int check_gerr(Ctx *x) {

@@ -40,6 +40,10 @@ long launches(int reset);
 
 inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
+// Wait for a stream by polling it with a deadline (PT_B200_WAIT_S seconds, default 120): a stream
+// that does not finish in time is reported as an error instead of blocking the caller forever.
+int wait_stream(cudaStream_t s);
+
 // ---- TMA tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point, so the
 // library does not link libcuda directly)
 int make_map_act(CUtensorMap *m, const float *base, int cin32, int64_t rows, int batch,

@@ -175,59 +175,6 @@ static int launch_win(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   return 0;
 }
 
-// Rows per CTA: the largest tile that does not cost extra waves on the SMs (a tile of MSUB*128
-// rows is modelled as MSUB + 0.5 units of time: mainloop plus fixed set-up/epilogue).
-static int pick_msub(const ConvLaunch &L, const int *cands, int ncand) {
-  static int forced = -2;
-  if (forced == -2) forced = getenv("PT_B200_MSUB") ? atoi(getenv("PT_B200_MSUB")) : 0;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  int best = cands[0];
-  double best_t = 1e300;
-  for (int i = 0; i < ncand; ++i) {
-    const int ms = cands[i];
-    if (forced > 0 && ms == forced) return ms;
-    const double tiles = (double)((L.g.m_rows + ms * kBM - 1) / (ms * kBM)) * (L.g.n_cols / L.bn) * L.batch;
-    const double waves = std::ceil(tiles / sms);
-    const double t = waves * (ms + 0.5);
-    if (t < best_t - 1e-9 || (std::fabs(t - best_t) < 1e-9 && ms > best)) {
-      best_t = t;
-      best = ms;
-    }
-  }
-  return best;
-}
-
-template <int BN>
-static int launch_pers(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
-  using P = PersCfg<BN>;
-  if (smem_optin(reinterpret_cast<const void *>(conv_tc_pers_kernel<BN>), P::kBytes)) return -1;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  CUtensorMap ta, tb;
-  if (make_map_act(&ta, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
-  if (make_map_w(&tb, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, BN)) return -1;
-  const long long tiles = (long long)((L.g.m_rows + kPMsub * kBM - 1) / (kPMsub * kBM)) *
-                          (L.g.n_cols / BN) * L.batch;
-  ConvGeom g = L.g;
-  g.nbatch = L.batch;
-  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-  conv_tc_pers_kernel<BN><<<grid, kPThreads, P::kBytes, st>>>(ta, tb, g, L.e, gerr);
-  PTB_CUDA(cudaGetLastError());
-  count_launch();
-  return 0;
-}
-
 template <int MODE, int F>
 static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   if (smem_optin(reinterpret_cast<const void *>(conv_tc_tn_kernel<MODE, F>), TNCfg<F>::kBytes))
@@ -258,9 +205,7 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   ConvGeom g = L.g;
   const long long mtl = (L.g.n_cols + kBM - 1) / kBM;
   g.tile_rows = kTNRows;
-  static int pick = -1;
-  if (pick < 0) pick = getenv("PT_B200_TILE_PICK") ? atoi(getenv("PT_B200_TILE_PICK")) : 1;
-  if (!L.g.tiles && pick) {
+  if (!L.g.tiles) {
     // The tile height whose last wave is fullest: waves x (rows + a per-tile cost of 16 rows,
     // the weight stream and pipeline fill) over heights 256 .. 160.
     long long best = -1;
@@ -336,25 +281,16 @@ int launch_conv(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   PTB_REQUIRE(L.g.m_rows > 0 && L.g.nkb > 0 && L.g.n_cols % L.bn == 0,
               "pt_b200: bad conv geometry (m=%d nkb=%d n=%d bn=%d)", L.g.m_rows, L.g.nkb,
               L.g.n_cols, L.bn);
-  static int no_win = -1;
-  if (no_win < 0) no_win = getenv("PT_B200_NO_WINDOW") ? atoi(getenv("PT_B200_NO_WINDOW")) : 0;
   const int halo = std::abs((L.g.ntap - 1) * L.g.row_step);
-  static int no_pers = -1;
-  if (no_pers < 0) no_pers = getenv("PT_B200_NO_PERSIST") ? atoi(getenv("PT_B200_NO_PERSIST")) : 0;
-  static int no_tn = -1;
-  if (no_tn < 0) no_tn = getenv("PT_B200_NO_TN") ? atoi(getenv("PT_B200_NO_TN")) : 0;
   if (L.g.tiles) {   // tile lists exist only in the channels-on-M kernel
     PTB_REQUIRE(L.bn == 128 && halo <= kWinHalo, "pt_b200: a conv tile list needs the channels-on-M kernel");
     return launch_tn(L, gerr, st);
   }
-  if (!no_win && halo <= kWinHalo) {
-    if (L.bn == 128) {
-      if (!no_tn) return launch_tn(L, gerr, st);
-      if (!no_pers) return launch_pers<128>(L, gerr, st);
-      static const int c24[] = {2, 4};
-      return pick_msub(L, c24, 2) == 2 ? launch_win<128, 2>(L, gerr, st)
-                                       : launch_win<128, 4>(L, gerr, st);
-    }
+  // Convs whose taps reach at most kWinHalo rows run on one activation window per 32-channel
+  // chunk: more than 64 output columns on the channels-on-M kernel, 16/32/64 on the time-on-M
+  // window kernel.  Wider reaches (only generic C-ABI calls) run the per-tap kernel.
+  if (halo <= kWinHalo) {
+    if (L.bn == 128) return launch_tn(L, gerr, st);
     switch (L.bn) {
       case 64: return launch_win<64, 2>(L, gerr, st);
       case 32: return launch_win<32, 2>(L, gerr, st);

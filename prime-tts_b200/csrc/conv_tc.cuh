@@ -559,330 +559,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 
 // ---------------------------------------------------------------------------------------------
-// Persistent variant: one CTA per SM walks a strided list of 256-row x BN-column tiles.
-//
-// Same window scheme as conv_tc_win_kernel (MSUB = 2), plus two TMEM accumulator sets (2 x 256
-// columns), so the epilogue of tile i runs while the tensor core works on tile i+1, and the TMA
-// producer runs ahead across tile boundaries.  Eight epilogue warps: warp w reads TMEM lane
-// quarter w % 4 (the rows) and column half w / 4; each thread issues its residual loads before
-// it waits for TMEM, so memory latency overlaps the accumulator read-out.
-constexpr int kPThreads = 320;   // warps 0-7 epilogue, 8 TMA producer, 9 TMEM allocator + MMA
-constexpr int kPMsub = 2;
-
-template <int BN>
-struct PersCfg {
-  static constexpr int kAccCols = 256;                           // one accumulator set: 2 x 128
-  static constexpr int kWinRows = kPMsub * kBM + kWinHalo;       // 320
-  static constexpr int kWinBytes = kWinRows * kBK * 4;           // 40 KiB
-  static constexpr int kB = BN * kBK * 4;
-  static constexpr int kBStagesRaw = (224 * 1024 - 2 * kWinBytes) / kB;
-  static constexpr int kBStages = kBStagesRaw > 8 ? 8 : kBStagesRaw;
-  static constexpr int kBytes = 2 * kWinBytes + kBStages * kB + 1024 + 256;
-  static constexpr int kChunks = (BN + 31) / 32;
-  static_assert(BN <= 128, "two accumulator sets of 2 x 128 columns fill TMEM");
-};
-
-// one 32-column chunk of one row: residual / accumulator inputs loaded before the TMEM read
-__device__ __forceinline__ void rows_chunk(const EpiParams &e, float (&v)[32], long long orow,
-                                           int col0, int n_base, unsigned char mk, int lim,
-                                           const float (&rs)[32], const float (&ac)[32]) {
-#pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 b = (e.bias && i < lim) ? __ldg(reinterpret_cast<const float4 *>(e.bias + n_base + i))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    v[i + 0] += b.x;
-    v[i + 1] += b.y;
-    v[i + 2] += b.z;
-    v[i + 3] += b.w;
-  }
-  if (e.res) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] += rs[i];
-  }
-  if (e.acc_mode == 2) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = ac[i] + v[i];
-  } else if (e.acc_mode == 3) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = div3_rn(ac[i] + v[i]);
-  }
-  const long long off = orow * e.ldc + col0;
-  if (e.out0) {
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      if (i >= lim) break;
-      *reinterpret_cast<float4 *>(e.out0 + off + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    }
-  }
-  if (e.out1) {
-    const long long off1 = orow * e.ldc1 + col0;
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      if (i >= lim) break;
-      const float4 w = make_float4(tf32_rna(leaky(v[i], e.alpha1)), tf32_rna(leaky(v[i + 1], e.alpha1)),
-                                   tf32_rna(leaky(v[i + 2], e.alpha1)), tf32_rna(leaky(v[i + 3], e.alpha1)));
-      *reinterpret_cast<float4 *>(e.out1 + off1 + i) = w;
-      if (mk & 2) *reinterpret_cast<float4 *>(e.out1 + off1 - 2LL * e.ldc1 + i) = w;
-    }
-  }
-}
-
-template <int BN>
-__global__ void __launch_bounds__(kPThreads, 1)
-    conv_tc_pers_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const ConvGeom g, const EpiParams e, uint32_t *gerr) {
-  using P = PersCfg<BN>;
-  constexpr int BS = P::kBStages;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t *gbase = smem_raw + (base - raw);
-  const uint32_t win0 = base, bst0 = base + 2 * P::kWinBytes;
-  const uint32_t bar0 = bst0 + BS * P::kB;
-  auto wfull = [&](int s) { return bar0 + 8u * s; };
-  auto wempty = [&](int s) { return bar0 + 8u * (2 + s); };
-  auto afull = [&](int s) { return bar0 + 8u * (4 + s); };
-  auto aempty = [&](int s) { return bar0 + 8u * (6 + s); };
-  auto bfull = [&](int s) { return bar0 + 8u * (8 + s); };
-  auto bempty = [&](int s) { return bar0 + 8u * (8 + BS + s); };
-  const uint32_t dbar = bar0 + 8u * (8 + 2 * BS);   // MMA drain on abort
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (9 + 2 * BS));
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kc = g.cin32 / kBK;
-  const int span = (g.ntap - 1) * g.row_step;
-  const int lo_off = span < 0 ? span : 0;
-  const int wrows = kPMsub * kBM + (span < 0 ? -span : span);
-  const int nbox = (wrows + kWinBox - 1) / kWinBox;
-  const int mt = (g.m_rows + kPMsub * kBM - 1) / (kPMsub * kBM);
-  const int nt = g.n_cols / BN;
-  const int ntiles = mt * nt * g.nbatch;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(wfull(s), 1);
-      mbar_init(wempty(s), 1);
-      mbar_init(afull(s), 1);
-      mbar_init(aempty(s), 8);   // one arrive per epilogue warp
-    }
-    for (int s = 0; s < BS; ++s) {
-      mbar_init(bfull(s), 1);
-      mbar_init(bempty(s), 1);
-    }
-    mbar_init(dbar, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 8 && lane == 0) {
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-  }
-  if (warp == 9) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 8) {
-    if (lane == 0) {
-      // ---------------- TMA producer, running ahead across tiles
-      int wiss[2] = {0, 0}, biss[BS];
-#pragma unroll
-      for (int s = 0; s < BS; ++s) biss[s] = 0;
-      bool ok = true;
-      int cw = 0, cb = 0;   // global window / weight-stage counters
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int z = t / (mt * nt), r = t - z * mt * nt, mi = r / nt, ni = r - mi * nt;
-        const int wlo = mi * (kPMsub * kBM) + g.row_off0 + lo_off;
-        for (int c = 0; c < kc && ok; ++c, ++cw) {
-          const int ws = cw & 1;
-          if (!mbar_wait(wempty(ws), ((cw >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
-            ok = false;
-            break;
-          }
-          const uint32_t wb = win0 + ws * P::kWinBytes;
-          mbar_expect_tx(wfull(ws), nbox * kWinBox * kBK * 4);
-          for (int b = 0; b < nbox; ++b)
-            tma_load_3d(wb + b * kWinBox * kBK * 4, &tmA, wfull(ws), c * kBK, wlo + b * kWinBox, z);
-          ++wiss[ws];
-          for (int k = 0; k < g.ntap; ++k, ++cb) {
-            const int bs = cb % BS;
-            if (!mbar_wait(bempty(bs), ((cb / BS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
-              ok = false;
-              break;
-            }
-            mbar_expect_tx(bfull(bs), P::kB);
-            tma_load_2d(bst0 + bs * P::kB, &tmB, bfull(bs), k * g.cin32 + c * kBK, ni * BN);
-            ++biss[bs];
-          }
-        }
-      }
-      if (!ok) {
-        for (int s = 0; s < 2; ++s)
-          if (wiss[s]) {
-            uint32_t it = 0;
-            while (!mbar_try_wait(wfull(s), (wiss[s] - 1) & 1) && ++it < kWaitLimit) {
-            }
-            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
-          }
-        for (int s = 0; s < BS; ++s)
-          if (biss[s]) {
-            uint32_t it = 0;
-            while (!mbar_try_wait(bfull(s), (biss[s] - 1) & 1) && ++it < kWaitLimit) {
-            }
-            if (it >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
-          }
-      }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      const uint32_t idesc = idesc_tf32(kBM, BN);
-      bool ok = true;
-      int cw = 0, cb = 0, it = 0, committed = 0;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
-        const int ab = it & 1;
-        if (!mbar_wait(aempty(ab), ((it >> 1) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t acc = tmem + ab * P::kAccCols;
-        for (int c = 0; c < kc && ok; ++c, ++cw) {
-          const int ws = cw & 1;
-          if (!mbar_wait(wfull(ws), (cw >> 1) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
-            ok = false;
-            break;
-          }
-          const uint32_t wb = win0 + ws * P::kWinBytes;
-          for (int k = 0; k < g.ntap; ++k, ++cb) {
-            const int bs = cb % BS;
-            if (!mbar_wait(bfull(bs), (cb / BS) & 1, abort_flag, gerr, ERR_WAIT_FULL)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint64_t db = sdesc_kmajor_sw128(bst0 + bs * P::kB);
-            const uint32_t arow = wb + (uint32_t)(k * g.row_step - lo_off) * (kBK * 4);
-#pragma unroll
-            for (int s = 0; s < kPMsub; ++s) {
-              const uint64_t da = sdesc_kmajor_sw128(arow + s * kBM * kBK * 4);
-#pragma unroll
-              for (int kk = 0; kk < kBK / 8; ++kk)
-                mma_tf32(acc + s * 128, da + 2u * kk, db + 2u * kk, idesc, (c | k | kk) != 0);
-            }
-            mma_commit(bempty(bs));
-          }
-          if (ok) mma_commit(wempty(ws));
-        }
-        if (ok) {
-          mma_commit(afull(ab));
-          ++committed;
-        }
-      }
-      if (!ok) {
-        // every MMA issued so far must finish before TMEM is released
-        mma_commit(dbar);
-        uint32_t n = 0;
-        while (!mbar_try_wait(dbar, 0) && ++n < kWaitLimit) {
-        }
-        if (n >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
-      }
-      (void)committed;
-    }
-  } else {
-    // ---------------- epilogue warps 0..7
-    const int q = warp & 3, half = warp >> 2;
-    constexpr int CH = P::kChunks;
-    constexpr int C0 = (CH + 1) / 2;         // chunks [0, C0) for half 0, [C0, CH) for half 1
-    const int jb = half ? C0 : 0, je = half ? CH : C0;
-    int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const int ab = it & 1;
-      if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
-      tc_fence_after();
-      const int z = t / (mt * nt), r = t - z * mt * nt, mi = r / nt, ni = r - mi * nt;
-      const int n0 = ni * BN;
-      const uint32_t tl = tmem + ab * P::kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-#pragma unroll 1
-      for (int s = 0; s < kPMsub; ++s) {
-        const int row = mi * (kPMsub * kBM) + s * kBM + q * 32 + lane;
-        if (e.mode == EPI_ROWS || e.mode == EPI_ROWS_CONVT) {
-          // row mapping and validity are per row: resolve once, load residuals early
-          long long orow = -1;
-          int rphase_base = 0;
-          bool valid = row < g.m_rows;
-          if (valid && e.mode == EPI_ROWS_CONVT) {
-            const int b = __ldg(e.obase + row);
-            valid = b != INT_MIN;
-            orow = (long long)b + (long long)e.s * row;   // + phase r per chunk
-          } else {
-            orow = row;
-          }
-          (void)rphase_base;
-#pragma unroll 1
-          for (int j = jb; j < je; ++j) {
-            const int n_base = n0 + 32 * j;
-            long long orow_j = orow;
-            int col0 = n_base;
-            if (e.mode == EPI_ROWS_CONVT) {
-              const int rr = n_base / e.cphase;
-              orow_j = orow + rr;
-              col0 = n_base - rr * e.cphase;
-            }
-            unsigned char mk = 0;
-            if (valid) mk = __ldg(e.mask + orow_j);
-            const int lim = e.nstore - col0 < 32 ? e.nstore - col0 : 32;
-            float rs[32], ac[32];
-            const long long off = orow_j * e.ldc + col0;
-            if ((mk & 1) && e.res) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (i < lim) r4 = *reinterpret_cast<const float4 *>(e.res + off + i);
-                rs[i] = r4.x; rs[i + 1] = r4.y; rs[i + 2] = r4.z; rs[i + 3] = r4.w;
-              }
-            }
-            if ((mk & 1) && e.acc_mode) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (i < lim) a4 = *reinterpret_cast<const float4 *>(e.accin + off + i);
-                ac[i] = a4.x; ac[i + 1] = a4.y; ac[i + 2] = a4.z; ac[i + 3] = a4.w;
-              }
-            }
-            float v[32];
-            tmem_ld32(tl + s * 128 + 32u * j, v);   // warp-collective: every lane takes part
-            if (mk & 1) rows_chunk(e, v, orow_j, col0, n_base, mk, lim, rs, ac);
-          }
-        } else {
-#pragma unroll 1
-          for (int j = jb; j < je; ++j) {
-            float v[32];
-            tmem_ld32(tl + s * 128 + 32u * j, v);
-            epilogue_chunk<BN>(e, v, z, row, g.m_rows, n0 + 32 * j);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(aempty(ab));
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-
-// ---------------------------------------------------------------------------------------------
 // Channels-on-M variant ("TN"): D[co][t] = W[co][k] . X[t][k].
 //
 // The MMA is M = 128 output channels (weights, A operand) x N = 256 time rows (the activation

@@ -300,6 +300,36 @@ namespace {
 // launch kinds reported by pt_b200_decoder_launch_times
 enum { LK_STAGE = 0, LK_CONV = 1, LK_CONVT = 2, LK_POST = 3, LK_TAIL = 4 };
 
+// channels-last rows [r0, r0 + L) x C of a [rows][ld] tensor -> channel-major [C][L]
+__global__ void unstage_rows_kernel(const float *__restrict__ src, int ld, long long r0,
+                                    long long L, int C, float *__restrict__ dst) {
+  __shared__ float tile[32][33];
+  const long long t0 = (long long)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const long long t = t0 + i;
+    const int c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (t < L && c < C) ? src[(r0 + t) * ld + c] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i;
+    const long long t = t0 + threadIdx.x;
+    if (c < C && t < L) dst[(long long)c * L + t] = tile[threadIdx.x][i];
+  }
+}
+
+// checkpoint `layer` (pt_b200_decoder_checkpoints): rows [r0, r0 + L) x C of a [rows][ld] tensor
+int ckpt(pt_b200_decoder *d, cudaStream_t st, int layer, const float *src, int ld, int C,
+         int64_t r0, int64_t L) {
+  if (!d->ck_dev) return 0;
+  dim3 grid((unsigned)((L + 31) / 32), (unsigned)((C + 31) / 32));
+  unstage_rows_kernel<<<grid, dim3(32, 8), 0, st>>>(src, ld, r0, L, C, d->ck_dev + d->ck_off[layer]);
+  PTB_CUDA(cudaGetLastError());
+  count_launch();
+  return 0;
+}
+
 // kind | (N tile << 8): the N tile names the conv kernel instance the launch used
 void rec(pt_b200_decoder *d, cudaStream_t st, int kind, double flops, double bytes, int bn = 0) {
   if (!d->prof || d->nrec >= pt_b200_decoder::kMaxRec) return;
@@ -319,11 +349,9 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
   // algorithmic work of one conv layer over every request's valid rows (2 x MACs)
   auto cflops = [&](double rows, int cin, int cout, int K) { return 2.0 * rows * cin * cout * K; };
   // every other conv launch walks its tiles last to first, starting on the rows its producer
-  // wrote last, which are still in L2 (PT_B200_ALT=0: all forward)
-  static int alt = -1;
-  if (alt < 0) alt = getenv("PT_B200_ALT") ? atoi(getenv("PT_B200_ALT")) : 1;
+  // wrote last, which are still in L2
   int nconv = 0;
-  auto rev = [&]() { return alt ? (nconv++ & 1) : 0; };
+  auto rev = [&]() { return nconv++ & 1; };
   // latents -> level-0 rows
   rec(d, st, LK_STAGE, 0.0, frames * 192 * 8);
   {
@@ -338,12 +366,14 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     EpiParams e = rows_epi(p.mask[0], 512);
     e.out1 = d->X0;
     if (run_conv(d, st, d->pre, d->Z, p.R[0], -3, 1, e, nullptr, 0, rev())) return -1;
+    if (ckpt(d, st, 0, d->X0, 512, 512, p.a[0][0], p.T[0])) return -1;
   }
   const float *lvl_in = d->X0;
   for (int s = 0; s < 2; ++s) {
     const int C = s == 0 ? 256 : 128;
     const int64_t rin = p.R[s], rout = p.R[s + 1];
     const unsigned char *mk = p.mask[s + 1];
+    const int64_t lo_rows = (s == 0 ? 4 : 16) * p.T[0];   // rows of request 0 (checkpoints)
     // ups.s: phase-decomposed convT, taps read delay-line rows g - j
     const double fin = frames * (s == 0 ? 1 : 4), fout = 4 * fin;
     rec(d, st, LK_CONVT, cflops(fin, 2 * C, C, 16), fin * 2 * C * 4 + fout * 2 * C * 4, d->ups[s].bn);
@@ -357,6 +387,8 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
       e.out0 = d->U[s];
       e.out1 = d->LU[s];
       if (run_conv(d, st, d->ups[s], lvl_in, rin, 0, -1, e, nullptr, 0, rev())) return -1;
+      if (ckpt(d, st, 1 + 19 * s, d->U[s], C, C, p.a[s + 1][0], (s == 0 ? 4 : 16) * p.T[0]))
+        return -1;
     }
     for (int rb = 0; rb < 3; ++rb) {
       const int r = 3 * s + rb, K = kK[rb];
@@ -368,6 +400,8 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
           const float *in = j == 0 ? d->LU[s] : d->XT[s];
           if (run_conv(d, st, d->rb1[r][j], in, rout, -kD[j] * (K - 1) / 2, kD[j], e, nullptr, 0,
                        rev()))
+            return -1;
+          if (ckpt(d, st, 2 + 19 * s + 6 * rb + 2 * j, d->H[s], C, C, p.a[s + 1][0], lo_rows))
             return -1;
         }
         // convs2 bytes: input + residual + outputs (+ the branch sum read by resblocks 1, 2)
@@ -399,6 +433,13 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
           }
           if (run_conv(d, st, d->rb2[r][j], d->H[s], rout, -(K - 1) / 2, 1, e, nullptr, 0, rev()))
             return -1;
+          if (d->ck_dev) {
+            const int li = 3 + 19 * s + 6 * rb + 2 * j;
+            const float *o = e.out0 ? e.out0 : e.out1;
+            const bool refl = j == 2 && rb == 2 && s == 1;   // the reflection-pad row in front
+            if (ckpt(d, st, li, o, C, C, p.a[s + 1][0] - (refl ? 1 : 0), lo_rows + (refl ? 1 : 0)))
+              return -1;
+          }
         }
       }
     }
@@ -411,6 +452,7 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     EpiParams e = rows_epi(p.mask_post, 80);
     e.out0 = d->POST;
     if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e, nullptr, 0, rev())) return -1;
+    if (ckpt(d, st, 39, d->POST, 80, 72, p.a[2][0] - 1, 16 * p.T[0] + 1)) return -1;
   }
   // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
   rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);
@@ -818,6 +860,76 @@ int pt_b200_decoder_launch_times(pt_b200_decoder *d, int max, double *ms, double
     kind[i] = d->rkind[i];
   }
   return n;
+}
+
+int pt_b200_decoder_checkpoints(pt_b200_decoder *d, const float *z_host, int64_t T,
+                                float *const *ckpt_host, float *wav_host) {
+  PTB_REQUIRE(d && z_host && ckpt_host && wav_host && T >= 2, "pt_b200: bad checkpoint arguments");
+  // element counts of the 40 layer outputs (include/pt_b200.h)
+  int64_t n[PT_B200_NCKPT];
+  n[0] = 512 * T;
+  for (int s = 0; s < 2; ++s) {
+    const int64_t C = s == 0 ? 256 : 128, L = (s == 0 ? 4 : 16) * T;
+    for (int i = 0; i < 19; ++i) n[1 + 19 * s + i] = C * L;
+  }
+  n[38] = 128 * (16 * T + 1);
+  n[39] = 72 * (16 * T + 1);
+  int64_t tot = 0;
+  for (int i = 0; i < PT_B200_NCKPT; ++i) {
+    d->ck_off[i] = tot;
+    tot += (n[i] + 63) & ~(int64_t)63;
+  }
+  std::lock_guard<std::mutex> lk(d->mu);
+  PTB_CUDA(cudaSetDevice(d->device));
+  cudaStream_t st = d->stream;
+  float *zd = nullptr, *wd = nullptr, *ck = nullptr;
+  auto release = [&]() {
+    d->ck_dev = nullptr;
+    cudaStreamSynchronize(st);
+    if (zd) cudaFree(zd);
+    if (wd) cudaFree(wd);
+    if (ck) cudaFree(ck);
+  };
+  int rc = -1;
+  do {
+    if (cudaMalloc(&zd, (size_t)T * 192 * 4) != cudaSuccess ||
+        cudaMalloc(&wd, (size_t)T * 256 * 4) != cudaSuccess ||
+        cudaMalloc(&ck, (size_t)tot * 4) != cudaSuccess) {
+      set_error("pt_b200: checkpoint buffers: out of device memory");
+      break;
+    }
+    if (cudaMemcpyAsync(zd, z_host, (size_t)T * 192 * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+      break;
+    pt_b200_window w{T, 0, T, 0, 256 * T, 0};
+    if (build_plan(d, st, 1, &w)) break;
+    d->ck_dev = ck;
+    if (run_decoder(d, st, zd, wd)) break;
+    d->ck_dev = nullptr;
+    if (cudaEventRecord(d->done, st) != cudaSuccess) break;
+    if (cudaMemcpyAsync(wav_host, wd, (size_t)T * 256 * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+      break;
+    bool ok = true;
+    for (int i = 0; i < PT_B200_NCKPT && ok; ++i)
+      if (ckpt_host[i])
+        ok = cudaMemcpyAsync(ckpt_host[i], ck + d->ck_off[i], (size_t)n[i] * 4,
+                             cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    if (!ok) break;
+    rc = 0;
+  } while (false);
+  if (rc) {
+    release();
+    return -1;
+  }
+  release();
+  // device errors of the decode (the error word) -- the lock is still held, so check here
+  PTB_CUDA(cudaMemcpy(d->gerr_host, d->gerr, 4, cudaMemcpyDeviceToHost));
+  if (*d->gerr_host) {
+    set_error("pt_b200: decoder device error word 0x%x", *d->gerr_host);
+    *d->gerr_host = 0;
+    cudaMemset(d->gerr, 0, 4);
+    return -1;
+  }
+  return 0;
 }
 
 int pt_v21_decode(pt_ctx *c, const pt_b200_decoder *d, const float *z, int64_t T, float *wav) {

@@ -136,6 +136,10 @@ struct pt_b200_decoder {
   float *az[2] = {}, *aw[2] = {};
   size_t az_bytes = 0, aw_bytes = 0;
   int async_next = 0;
+  // per-layer checkpoints (pt_b200_decoder_checkpoints): when ck_dev is set, a one-request decode
+  // copies each conv launch's output, channel-major, to ck_dev + ck_off[layer]
+  float *ck_dev = nullptr;
+  int64_t ck_off[PT_B200_NCKPT] = {};
   // live per-launch timing (pt_b200_decoder_profile): one event before each launch, one at the end
   static constexpr int kMaxRec = 64;
   bool prof = false;

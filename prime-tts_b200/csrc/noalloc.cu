@@ -12,6 +12,7 @@
 // kScratchBytes of it until the process exits.  Host code cannot use the variable's name as a
 // device address; the entry point asks the runtime for that address (cudaGetSymbolAddress) once
 // per device, the first time it runs on that device, with the device made current.
+#include <climits>
 #include <mutex>
 
 #include "../../include/pt_b200.h"
@@ -47,11 +48,26 @@ extern "C" int pt_b200_conv_noalloc(int device, void *stream, const float *x, in
   PTB_REQUIRE(x && y && wp && cin > 0 && T > 0 && ldx >= T && cout > 0 && K > 0 && dil > 0 &&
                   pad >= 0,
               "pt_b200_conv_noalloc: bad arguments");
+  // sizes are checked in 64-bit arithmetic before anything is narrowed to int: whatever does not
+  // fit the scratch array is rejected here, which also keeps every later int in range
   const int64_t Tout = T + 2 * (int64_t)pad - (int64_t)(K - 1) * dil;
   PTB_REQUIRE(Tout > 0, "pt_b200_conv_noalloc: empty output (T=%lld K=%d dil=%d pad=%d)",
               (long long)T, K, dil, pad);
+  PTB_REQUIRE(cin <= (int64_t)kScratchBytes && T <= (int64_t)kScratchBytes &&
+                  Tout <= (int64_t)INT_MAX && cout <= INT_MAX - 3,
+              "pt_b200_conv_noalloc: cin=%lld / T=%lld / Tout=%lld exceed the fixed scratch array",
+              (long long)cin, (long long)T, (long long)Tout);
+  const int64_t cin32l = round_up(cin, kBK);
+  const int64_t cout16 = round_up(cout, 16);
+  const int64_t need_l = (int64_t)kHeader + (int64_t)up256((size_t)(T * cin32l * 4)) +
+                         (int64_t)up256((size_t)(cout16 * K * cin32l * 4));
+  PTB_REQUIRE(need_l <= (int64_t)kScratchBytes,
+              "pt_b200_conv_noalloc: this conv needs at least %lld bytes of scratch, the fixed "
+              "array holds %zu (T x round_up(cin,32) + round_up(cout,16) x K x round_up(cin,32) "
+              "floats too large); use pt_v21_conv",
+              (long long)need_l, kScratchBytes);
   const int cout4 = (cout + 3) / 4 * 4;
-  const int cin32 = (int)round_up(cin, kBK);
+  const int cin32 = (int)cin32l;
   int bn = 0, n_pad = 0;
   if (pick_bn(cout4, &bn, &n_pad)) return -1;
   const size_t xbytes = up256((size_t)T * cin32 * 4);
@@ -128,9 +144,11 @@ extern "C" int pt_b200_conv_noalloc(int device, void *stream, const float *x, in
   L.e.a0 = a0;
   if (launch_conv(L, gerr, st)) return -1;
 
+  // synchronous: the error word is read back once the stream has finished (a bounded wait, like
+  // every other host wait of this library)
   uint32_t herr = 0;
   PTB_CUDA(cudaMemcpyAsync(&herr, gerr, 4, cudaMemcpyDeviceToHost, st));
-  PTB_CUDA(cudaStreamSynchronize(st));
+  if (wait_stream(st)) return -1;
   PTB_REQUIRE(herr == 0, "pt_b200_conv_noalloc: device error word 0x%x", herr);
   return 0;
 }

@@ -148,6 +148,7 @@ _SIGS = {
     "pt_b200_decoder_launch_times": ([C.c_void_p, C.c_int, C.POINTER(C.c_double),
                                       C.POINTER(C.c_double), C.POINTER(C.c_double),
                                       C.POINTER(C.c_int)], C.c_int),
+    "pt_b200_decoder_checkpoints": ([C.c_void_p, _f, _i64, C.POINTER(_f), _f], C.c_int),
     "pt_b200_conv_noalloc": ([C.c_int, C.c_void_p, C.c_void_p, _i64, _i64, _i64, C.c_void_p,
                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                               C.c_int, C.c_float], C.c_int),
@@ -692,6 +693,20 @@ class Decoder:
 
     def sync(self, stream=None) -> None:
         _check(lib().pt_b200_decoder_sync(self.h, stream), "pt_b200_decoder_sync")
+
+    def checkpoints(self, z: np.ndarray):
+        """pt_b200_decoder_checkpoints: one request's 40 per-layer outputs (channel-major, no gap
+        rows; shapes in include/pt_b200.h) and its waveform."""
+        z = np.ascontiguousarray(z, np.float32)
+        T = z.shape[-1]
+        shapes = [(512, T)] + [(256, 4 * T)] * 19 + [(128, 16 * T)] * 19 + [(72, 16 * T + 1)]
+        shapes[38] = (128, 16 * T + 1)
+        ck = [np.empty(sh, np.float32) for sh in shapes]
+        arr = (_f * len(ck))(*[_p(a) for a in ck])
+        wav = np.empty(256 * T, np.float32)
+        _check(lib().pt_b200_decoder_checkpoints(self.h, _p(z), T, arr, _p(wav)),
+               "pt_b200_decoder_checkpoints")
+        return ck, wav
 
     LAUNCH_KINDS = ("stage", "conv", "convT", "conv_post", "tail")
 

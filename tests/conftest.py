@@ -17,6 +17,20 @@ for p in (REPO, PKG, os.path.join(REPO, "oracle")):
         sys.path.insert(0, p)
 
 
+def reference_dir():
+    """The reference project's source tree: $PT_REFERENCE_DIR, else the `reference_path` recorded
+    in BASELINE.json; None when it is not on this machine (the GPU box has none)."""
+    import json
+    d = os.environ.get("PT_REFERENCE_DIR")
+    if not d:
+        try:
+            with open(os.path.join(REPO, "BASELINE.json")) as f:
+                d = json.load(f).get("reference_path")
+        except Exception:
+            d = None
+    return d if d and os.path.isdir(d) else None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA library)")
 

@@ -16,10 +16,12 @@ import numpy as np
 import pytest
 
 import pt_b200
+from conftest import reference_dir
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HDR = os.path.join(REPO, "include", "pt_b200.h")
-REF_HDR_DIR = "/root/reference/runtime/v21/src"
+_REF = reference_dir()
+REF_HDR_DIR = os.path.join(_REF, "runtime", "v21", "src") if _REF else None
 
 
 def declared_symbols():
@@ -77,7 +79,7 @@ def test_ctx_layout_matches_our_header_and_ctypes():
 
 
 def test_ctx_layout_matches_the_reference_header():
-    if not os.path.exists(os.path.join(REF_HDR_DIR, "pt_v21.h")):
+    if not REF_HDR_DIR or not os.path.exists(os.path.join(REF_HDR_DIR, "pt_v21.h")):
         pytest.skip("reference header not present on this machine")
     ref = _probe_offsets('#include "pt_v21.h"', REF_HDR_DIR)
     ours = _probe_offsets('#include "pt_b200.h"', os.path.join(REPO, "include"))

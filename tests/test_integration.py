@@ -8,16 +8,19 @@ import subprocess
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = "/root/reference/runtime/v21/src/pt_v21_host.c"
+from conftest import reference_dir
+
+_REF = reference_dir()
 
 
 def test_reference_interpreter_links_against_library():
-    if not os.path.exists(REF):
+    if not _REF:
         pytest.skip("reference sources not present on this machine")
     out = os.path.join(REPO, "oracle", "_ref", "pt_v21_b200")
     if os.path.exists(out):
         os.remove(out)
-    subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "interp"], check=True)
+    subprocess.run(["make", "-s", "-C", os.path.join(REPO, "oracle"), "interp", f"REF={_REF}"],
+                   check=True)
     assert os.path.exists(out)
     ldd = subprocess.run(["ldd", out], capture_output=True, text=True).stdout
     assert "libpt_b200.so" in ldd and "not found" not in ldd

@@ -5,9 +5,11 @@ allocator, a process with a fixed device footprint) hands over device buffers fo
 weights, bias and output; the library takes its scratch from a fixed array compiled into it
 instead of calling cudaMalloc.  This test calls that entry point through the C ABI twice in a
 row -- the second call on a different shape, so stale contents of the shared array from the
-first call would show -- and compares each result with the allocating entry point pt_v21_conv
-within the per-op tolerance the other tests use.  It lives in its own file, collected last, and
-sets up everything it needs itself, so it also passes alone in a fresh process.
+first call would show -- and compares each result with the CPU oracle's conv (the reference's
+pt_v21_conv_cpu restated) and with the allocating entry point pt_v21_conv, within the per-op
+tolerance the other tests use; repeated calls must leave the device's free memory unchanged.  It
+lives in its own file, collected last, and sets up everything it needs itself, so it also passes
+alone in a fresh process.
 """
 import ctypes as C
 
@@ -46,15 +48,49 @@ def test_noalloc_matches_allocating_conv_twice():
         (71, 512, 256, 7, 1, 256, 1, 0.1),     # the BASELINE config-1 shape
         (72, 96, 72, 11, 3, 150, 0, 0.0),      # smaller, ragged: stale scratch would show
     ]
+    orc = oracle.CpuDecoder("oracle")
     with pt_b200.Context(0) as ctx:
         for seed, cin, cout, K, dil, T, e0, a0 in cases:
             x, wp, b = conv_inputs(seed, 1, cin, cout, K, T)
             pad = dil * (K - 1) // 2
+            want = orc.conv(x, wp, b, cout, K, pad, dil, epi0=e0, a0=a0)[0]
             ref = ctx.conv(x, wp, b, cout, K, pad, dil, epi0=e0, a0=a0)[0]
             y = _noalloc(x[0], wp, b, cout, K, pad, dil, e0, a0)
-            m = oracle.metrics(y, ref)
             assert np.isfinite(y).all()
-            assert m["max_rel"] <= TOL, (seed, m)
+            m = oracle.metrics(y, want)
+            assert m["max_rel"] <= TOL, (seed, "vs oracle", m)
+            m = oracle.metrics(y, ref)
+            assert m["max_rel"] <= TOL, (seed, "vs pt_v21_conv", m)
+
+
+def test_noalloc_allocates_no_device_memory():
+    """After a warm-up call, further calls of both shapes leave cudaMemGetInfo's free bytes as
+    they were (torch's caching allocator is idle meanwhile, so a change would be the library's)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bufs = []
+    for seed, cin, cout, K, dil, T in ((73, 512, 256, 7, 1, 256), (74, 96, 72, 11, 3, 150)):
+        x, wp, b = conv_inputs(seed, 1, cin, cout, K, T)
+        Tout = T + 2 * (dil * (K - 1) // 2) - (K - 1) * dil
+        bufs.append((torch.from_numpy(x[0]).to(dev), torch.from_numpy(wp.ravel()).to(dev),
+                     torch.from_numpy(b).to(dev), torch.empty(((cout + 3) // 4 * 4, Tout), device=dev),
+                     cin, T, cout, K, dil))
+    torch.cuda.synchronize()
+
+    def call(xd, wd, bd, yd, cin, T, cout, K, dil):
+        rc = pt_b200.lib().pt_b200_conv_noalloc(0, None, xd.data_ptr(), T, cin, T, yd.data_ptr(),
+                                                cout, K, dil * (K - 1) // 2, dil, wd.data_ptr(),
+                                                bd.data_ptr(), 0, C.c_float(0.0))
+        assert rc == 0, pt_b200.lib().pt_b200_last_error()
+
+    for bb in bufs:   # warm-up: the first call on the device looks up the array's address
+        call(*bb)
+    free0, _ = torch.cuda.mem_get_info(dev)
+    for _ in range(3):
+        for bb in bufs:
+            call(*bb)
+    free1, _ = torch.cuda.mem_get_info(dev)
+    assert free1 == free0, (free0, free1)
 
 
 def test_noalloc_rejects_oversized_calls():
