@@ -49,6 +49,7 @@ import pt_b200  # noqa: E402
 METRIC = "decoder audio-sec/s per box"
 UNIT = "audio-s/s"
 PER_GPU_REQUESTS = 64
+SMS = 148
 SAMPLE_RATE = 16000
 HOP = 256
 
@@ -91,6 +92,12 @@ def parse():
                     help="config 5: carried state (default) or re-decoded widened windows")
     ap.add_argument("--layers", action="store_true",
                     help="print the per-layer table of one decode instead of the bench line")
+    ap.add_argument("--no-stream", action="store_true",
+                    help="skip the config-5 sub-block of the batch workload's line")
+    ap.add_argument("--no-distinct", action="store_true",
+                    help="skip the distinct-batches e2e figure")
+    ap.add_argument("--mma-rate", action="store_true",
+                    help="print the live tcgen05 kind::tf32 rate of GPU 0 and exit")
     ap.add_argument("--traffic-from", default=None,
                     help="ncu CSV with dram__bytes_{read,write}.sum of conv_tc_tn_kernel launches")
     return ap.parse_args()
@@ -316,25 +323,14 @@ def layer_table(recs, steps):
 
 
 # ----------------------------------------------------------------------------------------------
-def cpu_reference_sample(T, zs, w, threads):
-    """Bounded sample for the reference CPU decoder: one request per host thread, taken from the
-    16 shortest requests of the workload (cycled), all threads in parallel."""
-    order = sorted(range(len(T)), key=lambda i: T[i])[:16]
-    return [order[i % len(order)] for i in range(threads)]
-
-
-def run_cpu_reference(T, zs, w, picks):
-    import oracle
-    kind = "reference" if os.path.exists(oracle.LIB_REF) else "oracle"
-    decs = [oracle.CpuDecoder(kind) for _ in picks]
-    t0 = time.perf_counter()
-    ths = [threading.Thread(target=d.decode, args=(w, zs[i])) for d, i in zip(decs, picks)]
-    for t in ths:
-        t.start()
-    for t in ths:
-        t.join()
-    dt = time.perf_counter() - t0
-    return audio_seconds(sum(T[i] for i in picks)) / dt, dt, ("reference" if kind == "reference" else "port")
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
 
 
 def host_threads():
@@ -344,14 +340,74 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def cpu_sample(T, threads, steps):
+    """The CPU arms' bounded sample: per step `threads` requests, one from each of `threads` equal
+    bands of the workload sorted by T, the member of each band rotating with the step -- so every
+    step spans the T distribution and all requests are decoded every len(T)/threads steps."""
+    order = sorted(range(len(T)), key=lambda i: T[i])
+    nb = min(threads, len(T))
+    picks = []
+    for k in range(steps):
+        for b in range(nb):
+            lo, hi = (b * len(T)) // nb, ((b + 1) * len(T)) // nb
+            picks.append(order[lo + k % max(1, hi - lo)])
+    return picks
+
+
+def run_cpu_queue(T, zs, w, picks, threads):
+    """Decode `picks` with `threads` host threads pulling whole requests from one queue, longest
+    first: the reference's one-request-per-thread model (main_v21_par.c) with every thread kept
+    busy, as a server keeps them.  Returns (audio-s/s, wall s, kind)."""
+    import oracle
+    kind = "reference" if os.path.exists(oracle.LIB_REF) else "oracle"
+    decs = [oracle.CpuDecoder(kind) for _ in range(threads)]
+    queue = sorted(picks, key=lambda i: -T[i])
+    lock, nxt = threading.Lock(), [0]
+
+    def worker(d):
+        while True:
+            with lock:
+                if nxt[0] >= len(queue):
+                    return
+                i = queue[nxt[0]]
+                nxt[0] += 1
+            d.decode(w, zs[i])
+
+    ths = [threading.Thread(target=worker, args=(d,)) for d in decs]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    return audio_seconds(sum(T[i] for i in picks)) / dt, dt, ("reference" if kind == "reference" else "port")
+
+
+def cpu_warmup(T, zs, w, threads):
+    """One short request per thread (page faults, allocator pools), untimed."""
+    short = sorted(range(len(T)), key=lambda i: T[i])[:1] * threads
+    run_cpu_queue(T, zs, w, short, threads)
+
+
+def cpu_sample_text(T, picks, steps, threads):
+    tp = [T[i] for i in picks]
+    return (f"{len(picks) // steps} config-4 requests per step ({sum(tp) // steps} frames), one from "
+            f"each of {threads} T-bands of the {len(T)}, rotating so every request is decoded every "
+            f"{max(1, len(T) // threads)} steps (T {min(tp)}..{max(tp)} over the run); {threads} host "
+            f"threads pull whole requests from one queue, longest first; CPU: {cpu_model()}, "
+            f"nproc {os.cpu_count()}")
+
+
 def cpu_baseline_block(T, zs, w):
     threads = host_threads()
-    picks = cpu_reference_sample(T, zs, w, threads)
-    v, dt, kind = run_cpu_reference(T, zs, w, picks)
-    tp = sorted(set(T[i] for i in picks))
+    cpu_warmup(T, zs, w, threads)
+    # two steps' requests in one queue: longest first, so the shorter half fills in behind the
+    # longer one and every thread stays busy to the end
+    picks = cpu_sample(T, threads, 2)
+    v, dt, kind = run_cpu_queue(T, zs, w, picks, threads)
     return {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{len(picks)} config-4 requests (T in {tp[0]}..{tp[-1]} frames, the 16 "
-                      f"shortest cycled), one per host thread in parallel; {dt:.1f} s wall"}
+            "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+            "sample": cpu_sample_text(T, picks, 2, threads) + f"; 2 steps, {dt:.1f} s wall"}
 
 
 def reference_arm(args):
@@ -359,27 +415,24 @@ def reference_arm(args):
     if rank != 0:
         return 0
     T, zs, w = workload(args.gpus)
+    T1 = T   # the whole job's requests (64 per GPU) are the population the sample spans
     threads = host_threads()
-    picks = cpu_reference_sample(T, zs, w, threads)
     for _ in range(args.warmup):
-        run_cpu_reference(T, zs, w, picks)
-    times, kind = [], "reference"
-    for _ in range(args.steps):
-        v, dt, kind = run_cpu_reference(T, zs, w, picks)
-        times.append(dt)
-    per_step = audio_seconds(sum(T[i] for i in picks))
-    value = per_step / statistics.mean(times)
-    tp = sorted(set(T[i] for i in picks))
-    sample = (f"{len(picks)} config-4 requests per step (T in {tp[0]}..{tp[-1]}, the 16 shortest "
-              f"cycled), one per host thread")
+        cpu_warmup(T1, zs, w, threads)
+    picks = cpu_sample(T1, threads, args.steps)
+    value, dt, kind = run_cpu_queue(T1, zs, w, picks, threads)
+    sample = cpu_sample_text(T1, picks, args.steps, threads)
     emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * statistics.mean(times), 2), "higher_is_better": True,
+        "ms_per_step": round(1e3 * dt / args.steps, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args.gpus, T),
+        "sample": {"requests_per_step": len(picks) // args.steps,
+                   "frames_per_step": sum(T1[i] for i in picks) // args.steps,
+                   "requests_decoded": len(picks), "wall_s": round(dt, 2)},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "nproc": os.cpu_count(), "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })
@@ -394,6 +447,11 @@ def main():
         return traffic_from_csv(args.traffic_from)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.mma_rate:
+        runs = [pt_b200.mma_rate(0) for _ in range(5)]
+        emit({"mma_rate": runs, "note": "tcgen05.mma kind::tf32 M128 N256 K8, operands in shared "
+              "memory, one CTA per SM (pt_b200_mma_rate, iters 20000)"})
+        return 0
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -471,6 +529,18 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather_ranks(vals):
+        """[[v0, v1, ...] of every rank] (float64 over NCCL; outside any timed region)."""
+        if not dist:
+            return [list(vals)]
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
+    # the tensor core's kind::tf32 rate on this GPU, measured live (the conv roofline's denominator)
+    mma = pt_b200.mma_rate(local)
+
     # ---- device-resident throughput ----------------------------------------------------------
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
@@ -497,7 +567,9 @@ def main():
     gpu_launches = pt_b200.kernel_launches()
     barrier()
     dec.profile(False)
-    t_step = max_over_ranks(total_ms / args.steps) / 1e3
+    clk = clocks.stop(list(range(world))) if rank == 0 else None
+    per_rank = gather_ranks([rank, len(T), int(T.sum()), total_ms / args.steps])
+    t_step = max(r[3] for r in per_rank) / 1e3
 
     # ---- end to end through the host entry point (pinned buffers, copies timed) --------------
     z_host = torch.from_numpy(zcat).pin_memory()
@@ -530,6 +602,7 @@ def main():
     barrier()
     t_e2e = max_over_ranks(e2e_ms / args.steps) / 1e3
     t_e2e_sync = None
+    distinct = None
     if kind == "batch":
         # Pipelined, as a server runs it (pt_b200_decode_batch_async): step k+1's upload and step
         # k's download overlap step k's decode.  One timed region from the first upload to the
@@ -537,24 +610,56 @@ def main():
         # every decode, inside the timed region.
         up, decs, down = dec.async_streams()
         s_up, s_dec, s_down = (torch.cuda.ExternalStream(h, device=dev) for h in (up, decs, down))
+
+        def pipelined(batches):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(s_up)
+            for Tb, zb, wb in batches:
+                with torch.cuda.stream(s_dec):
+                    flush.fill_(1.0)
+                dec.decode_async(Tb, zb.data_ptr(), wb.data_ptr())
+            e1.record(s_down)
+            dec.decode_async_wait()
+            return e0.elapsed_time(e1)
+
         for _ in range(2):   # warm-up: both staging slots captured as graphs
             dec.decode_async(T, z_host.data_ptr(), wav_host.data_ptr())
         dec.decode_async_wait()
         barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(s_up)
-        for _ in range(args.steps):
-            with torch.cuda.stream(s_dec):
-                flush.fill_(1.0)
-            dec.decode_async(T, z_host.data_ptr(), wav_host.data_ptr())
-        e1.record(s_down)
-        dec.decode_async_wait()
+        ms = pipelined([(T, z_host, wav_host)] * args.steps)
         barrier()
         t_e2e_sync = t_e2e
-        t_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps) / 1e3
-    clk = clocks.stop(list(range(world))) if rank == 0 else None
+        t_e2e = max_over_ranks(ms / args.steps) / 1e3
+        if not args.no_distinct:
+            # A new ragged batch every step (config-4 draws of seeds 3, 13, 23, ...; none repeats),
+            # as a server sees them: plan building and eager launches inside the timed region.
+            draws, audio_d = [], 0.0
+            for k in range(args.steps + 2):
+                Tk_all, zk_all = pt_b200.config4(seed=3 + 10 * k, n=PER_GPU_REQUESTS * world)
+                sk = lpt_shards(Tk_all, world)[rank]
+                Tk = np.array([Tk_all[i] for i in sk], np.int64)
+                zk = torch.from_numpy(np.concatenate([zk_all[i].ravel() for i in sk])).pin_memory()
+                wk = torch.empty(int(HOP * Tk.sum()), dtype=torch.float32).pin_memory()
+                draws.append((Tk, zk, wk))
+                if k >= 2:
+                    audio_d += audio_seconds(sum(Tk_all))
+            pipelined(draws[:2])   # warm-up
+            barrier()
+            ms = pipelined(draws[2:])
+            barrier()
+            t_d = max_over_ranks(ms) / 1e3
+            distinct = {"value": round(audio_d / t_d, 1), "ms_per_step": round(t_d / args.steps * 1e3, 3),
+                        "batches": args.steps,
+                        "mode": "pipelined like `value`, a different config-4 draw every step "
+                                "(seeds 3 + 10k): plan building and eager launches timed"}
     ok = np.isfinite(wav_host.numpy()).all()
+
+    # ---- config 5 alongside the batch workload (carried-state streaming, per-rank shards) -----
+    stream_block = None
+    if kind == "batch" and not args.no_stream:
+        stream_block = measure_stream(args, world, rank, local, dec, stream, flush, barrier,
+                                      gather_ranks)
 
     if dist:
         dist.destroy_process_group()
@@ -582,21 +687,35 @@ def main():
     tot = sum(g[0] for g in groups.values())
     dom = max(groups, key=lambda k: groups[k][0])
     peaks, peak_src = measured_peaks()
-    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    # kind::tf32 issues at half the kind::f16 rate; the timed region is a fraction of a second,
+    # so the burst cuBLAS figure is the denominator (the sustained one is reported beside it)
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    tf32_sus = peaks["bf16_tflops_sustained"] / 2.0
+    # the tensor pipe's own rate, measured live by the probe at the clock a tensor-saturating load
+    # holds on this GPU (the sampled clock of the short timed region is beside it, for reference)
+    mma_peak = mma["tflops"]
+    sm_mhz = (clk or {}).get("sm_mhz")
     g = groups[dom]
     if dom.startswith("conv_tc"):
         achieved = g[1] / (g[0] / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tf32_peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
-                "traffic": traffic_from_profiles(dom, g[1] / g[3])}
+                "traffic": traffic_from_profiles(dom, g[1] / g[3]),
+                "frac_sustained": round(achieved / tf32_sus, 4),
+                "frac_mma": round(achieved / mma_peak, 4)}
     else:
         achieved = g[2] / (g[0] / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None}
     roof["kernel"] = dom
     roof["share"] = round(g[0] / tot, 4)
-    roof["peak_source"] = (f"{peak_src} MEASURED_PEAKS bf16_tflops_sustained "
-                           f"{peaks['bf16_tflops_sustained']} / 2 (kind::tf32 rate)")
+    roof["peak_source"] = (f"{peak_src} MEASURED_PEAKS bf16_tflops {peaks['bf16_tflops']} / 2 "
+                           f"(burst; kind::tf32 runs at half the kind::f16 rate); frac_sustained: "
+                           f"bf16_tflops_sustained {peaks['bf16_tflops_sustained']} / 2; frac_mma: "
+                           f"the live tcgen05 kind::tf32 probe (pt_b200_mma_rate), "
+                           f"{mma['flop_per_clk_sm']:.0f} FLOP/clk/SM x {SMS} SMs at the "
+                           f"{mma['sm_mhz']:.0f} MHz it held = {mma_peak:.1f} TFLOP/s; median SM clock "
+                           f"sampled in the timed region: {sm_mhz} MHz")
     conv_ms = sum(v[0] for k, v in groups.items() if k.startswith("conv_tc"))
     conv_fl = sum(v[1] for k, v in groups.items() if k.startswith("conv_tc"))
     conv_tflops = conv_fl / (conv_ms / 1e3) / 1e12
@@ -614,19 +733,26 @@ def main():
         "config": config_dict(world, T_all, kind, args.stream_scheme),
         "conv_tflops": round(conv_tflops, 1),
         "conv_tf32_frac": round(conv_tflops / tf32_peak, 4),
+        "conv_tf32_frac_mma": round(conv_tflops / mma_peak, 4),
         "roofline": roof,
+        "mma_probe": {k: round(v, 1) for k, v in mma.items()},
         "kernels": kernels,
+        "ranks": [{"rank": int(r[0]), "requests": int(r[1]), "frames": int(r[2]),
+                   "ms_per_step": round(r[3], 3)} for r in per_rank],
         "e2e": {"value": round(audio / t_e2e, 1), "unit": UNIT,
                 "h2d_bytes_per_step": int(zcat.nbytes), "d2h_bytes_per_step": int(wav_host.numel() * 4),
                 "ms_per_step": round(t_e2e * 1e3, 3), "output_finite": bool(ok),
                 "mode": ("pipelined host-buffer decodes (pt_b200_decode_batch_async: upload of "
                          "step k+1 and download of step k overlap decode k), one timed region, "
-                         "L2 flushed before every decode inside it") if kind == "batch" else
+                         "L2 flushed before every decode inside it; the same batch every step") if kind == "batch" else
                         "per step: upload, decode, download, synchronised",
-                "sync_value": round(audio / t_e2e_sync, 1) if t_e2e_sync else None},
+                "sync_value": round(audio / t_e2e_sync, 1) if t_e2e_sync else None,
+                "distinct_batches": distinct},
         "gpu_launches": int(gpu_launches),
         "clocks": clk,
     }
+    if stream_block is not None:
+        out["stream"] = stream_block
     if carry is not None:
         out["roofline"]["note"] = ("whole step: every decoder FLOP of the step over its device "
                                    "time, tail and staging included")
@@ -639,6 +765,54 @@ def main():
     dec.close()
     emit(out)
     return 0
+
+
+def measure_stream(args, world, rank, local, dec, stream, flush, barrier, gather_ranks):
+    """BASELINE config 5 on this rank's share (512 streams per GPU, LPT on frames), carried state:
+    every pass a replayed graph after the first run; useful (emitted) audio-s/s of the whole job,
+    device time as the max over ranks; warm-up >= 3 runs, L2 flushed before every timed run."""
+    import torch
+    dev = torch.device("cuda", local)
+    T_all, zs_all = pt_b200.config5(seed=4, n=PER_GPU_STREAMS * world)
+    shard = lpt_shards(T_all, world)[rank]
+    T = np.array([T_all[i] for i in shard], np.int64)
+    z = torch.from_numpy(np.concatenate([zs_all[i].ravel() for i in shard])).to(dev)
+    wav = torch.empty(int(HOP * T.sum()), device=dev)
+    chunk = pt_b200.STREAM_WIN - 2 * pt_b200.STREAM_CTX
+    sess = pt_b200.CarrySession(dec, T, chunk)
+    sh = stream.cuda_stream
+    steps = max(3, min(args.steps, 5))
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            sess.run_all(z.data_ptr(), wav.data_ptr(), sh)
+        dec.sync(sh)
+    barrier()
+    ms = 0.0
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            flush.fill_(1.0)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            sess.run_all(z.data_ptr(), wav.data_ptr(), sh)
+            e1.record(stream)
+            dec.sync(sh)
+            ms += e0.elapsed_time(e1)
+    barrier()
+    finite = bool(torch.isfinite(wav).all().item())
+    passes = sess.passes
+    sess.close()
+    per_rank = gather_ranks([rank, len(T), int(T.sum()), ms / steps, passes])
+    t = max(r[3] for r in per_rank) / 1e3
+    audio = audio_seconds(sum(T_all))
+    return {"workload": "BASELINE config 5: 512 streams per GPU, T~U{100..1000} (seed 4), 32 new "
+                        "frames per stream per pass, carried state (output equals a whole-utterance "
+                        "decode); streams sharded whole across GPUs (LPT on frames)",
+            "metric": "useful audio-sec/s per box", "value": round(audio / t, 1), "unit": UNIT,
+            "streams": len(T_all), "frames": int(sum(T_all)), "steps": steps,
+            "ms_per_step": round(t * 1e3, 3), "output_finite": finite,
+            "ranks": [{"rank": int(r[0]), "streams": int(r[1]), "frames": int(r[2]),
+                       "ms_per_step": round(r[3], 3), "passes": int(r[4])} for r in per_rank]}
 
 
 if __name__ == "__main__":

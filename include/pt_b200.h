@@ -406,6 +406,13 @@ PT_B200_API int pt_b200_conv_noalloc(int device, void *stream, const float *x, i
                                      int dil, const float *wp, const float *bias, int epi0,
                                      float a0);
 
+/* The tensor core's kind::tf32 rate on `device`, measured live (the conv stack's roofline): one
+ * CTA per SM issues `iters` x 4 MMAs of M128 x N256 x K8 from shared-memory operands into TMEM.
+ * Returns FLOP per SM clock (averaged over the SMs), the aggregate TFLOP/s over the run, and the
+ * SM clock the run held (MHz).  Synchronous; about 5 ms at iters = 20000. */
+PT_B200_API int pt_b200_mma_rate(int device, int iters, double *flop_per_clk_sm, double *tflops,
+                                 double *sm_mhz);
+
 /* Diagnostics: the last error message of the calling thread, and the number of this library's
  * kernels launched by the calling thread since the last reset. */
 PT_B200_API const char *pt_b200_last_error(void);

@@ -482,7 +482,7 @@ void pt_b200_carry_close(pt_b200_carry *c) {
   for (auto &G : c->graphs)
     if (G.exec) cudaGraphExecDestroy(G.exec);
   if (c->block) cudaFree(c->block);
-  if (c->lay.table_block) cudaFree(c->lay.table_block);
+  free_plan(c->lay);
   delete c;
 }
 

@@ -170,27 +170,53 @@ int ptb::dec::build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_win
     t[7 * nreq + i] = w[i].keep_lo;
     t[8 * nreq + i] = w[i].keep_hi;
   }
-  // one device block: masks, convT row maps, per-request tables
+  // gap-row ranges of every level: before the first request, between requests, after the last
+  std::vector<long long> gap((size_t)3 * (nreq + 1) * 2);
+  for (int l = 0; l < 3; ++l) {
+    long long *g = gap.data() + (size_t)l * (nreq + 1) * 2;
+    int64_t prev = 0;
+    for (int i = 0; i <= nreq; ++i) {
+      const int64_t next = i < nreq ? a[l][i] : p.R[l];
+      g[2 * i] = prev;
+      g[2 * i + 1] = next - prev;
+      if (i < nreq) prev = a[l][i] + scale[l] * T[i];
+    }
+  }
+  // one device block: masks, convT row maps, per-request tables, gap ranges
   auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
-  size_t off[8], tot = 0;
-  const size_t sz[8] = {(size_t)p.R[0], (size_t)p.R[1], (size_t)p.R[2], (size_t)p.R[2],
-                        (size_t)p.R[2], ob01.size() * 4, ob12.size() * 4, tab.size() * 8};
-  for (int k = 0; k < 8; ++k) {
+  size_t off[9], tot = 0;
+  const size_t sz[9] = {(size_t)p.R[0], (size_t)p.R[1], (size_t)p.R[2], (size_t)p.R[2],
+                        (size_t)p.R[2], ob01.size() * 4, ob12.size() * 4, tab.size() * 8,
+                        gap.size() * 8};
+  for (int k = 0; k < 9; ++k) {
     off[k] = tot;
     tot += al(sz[k]);
   }
-  PTB_CUDA(cudaMalloc(&p.table_block, tot));
+  if (tot > p.table_cap) {
+    // grow with headroom, so that later plans of similar batches reuse the buffers
+    if (p.table_block) cudaFree(p.table_block);
+    if (p.host_stage) cudaFreeHost(p.host_stage);
+    p.table_block = p.host_stage = nullptr;
+    p.table_cap = 0;
+    const size_t cap = al(tot + tot / 4);
+    PTB_CUDA(cudaMalloc(&p.table_block, cap));
+    PTB_CUDA(cudaMallocHost(&p.host_stage, cap));
+    p.table_cap = cap;
+  }
   char *base = static_cast<char *>(p.table_block);
-  std::vector<char> host(tot, 0);
-  std::memcpy(host.data() + off[0], m[0].data(), sz[0]);
-  std::memcpy(host.data() + off[1], m[1].data(), sz[1]);
-  std::memcpy(host.data() + off[2], m[2].data(), sz[2]);
-  std::memcpy(host.data() + off[3], mr.data(), sz[3]);
-  std::memcpy(host.data() + off[4], mp.data(), sz[4]);
-  std::memcpy(host.data() + off[5], ob01.data(), sz[5]);
-  std::memcpy(host.data() + off[6], ob12.data(), sz[6]);
-  std::memcpy(host.data() + off[7], tab.data(), sz[7]);
-  PTB_CUDA(cudaMemcpyAsync(base, host.data(), tot, cudaMemcpyHostToDevice, st));
+  char *host = static_cast<char *>(p.host_stage);
+  std::memcpy(host + off[0], m[0].data(), sz[0]);
+  std::memcpy(host + off[1], m[1].data(), sz[1]);
+  std::memcpy(host + off[2], m[2].data(), sz[2]);
+  std::memcpy(host + off[3], mr.data(), sz[3]);
+  std::memcpy(host + off[4], mp.data(), sz[4]);
+  std::memcpy(host + off[5], ob01.data(), sz[5]);
+  std::memcpy(host + off[6], ob12.data(), sz[6]);
+  std::memcpy(host + off[7], tab.data(), sz[7]);
+  std::memcpy(host + off[8], gap.data(), sz[8]);
+  // from pinned memory: asynchronous, ordered before every later launch on `st`
+  PTB_CUDA(cudaMemcpyAsync(base, host, tot, cudaMemcpyHostToDevice, st));
+  p.gap = reinterpret_cast<long long *>(base + off[8]);
   for (int l = 0; l < 3; ++l) p.mask[l] = reinterpret_cast<unsigned char *>(base + off[l]);
   p.mask_refl = reinterpret_cast<unsigned char *>(base + off[3]);
   p.mask_post = reinterpret_cast<unsigned char *>(base + off[4]);
@@ -210,32 +236,37 @@ int ptb::dec::build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_win
   return 0;
 }
 
+void ptb::dec::free_plan(Plan &p) {
+  if (p.table_block) cudaFree(p.table_block);
+  if (p.host_stage) cudaFreeHost(p.host_stage);
+  if (p.used) cudaEventDestroy(p.used);
+  p = Plan();
+}
+
 namespace {
 
-// Lay the requests out (masks, convT row maps, per-request tables) unless the previous plan had
-// the same requests.  A new plan first waits for the last decode that used the old one (any
-// stream), then uploads and zeroes on `st`, so later work on `st` is ordered after it.
-int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_window *w) {
-  Plan &p = d->plan;
-  if (d->have_plan && same_windows(p.W, nreq, w)) return 0;
-  if (check_windows(nreq, w)) return -1;
-  if (d->done) PTB_CUDA(cudaEventSynchronize(d->done));
-  if (p.table_block) cudaFree(p.table_block);
-  d->have_plan = false;
-  p = Plan();
-  ++d->plan_id;
-  if (build_layout(p, st, nreq, w)) return -1;
+// Zero every gap row of the activation tensors: one block per (gap range, tensor); a gap range of
+// a channels-last tensor is one contiguous run of rows x C floats (C a multiple of 4).
+struct GapTargets {
+  float *t[3][8];
+  int c[3][8];
+  int nt[3];
+};
 
-  // activation buffers: grow if needed, then zero (gap rows must read as zeros)
+__global__ void zero_gaps_kernel(const long long *__restrict__ gap, int nrange, GapTargets tg) {
+  const int l = blockIdx.x / nrange, r = blockIdx.x - l * nrange;
+  if (blockIdx.y >= (unsigned)tg.nt[l]) return;
+  const long long *g = gap + ((long long)l * nrange + r) * 2;
+  const int C = tg.c[l][blockIdx.y];
+  float4 *dst = reinterpret_cast<float4 *>(tg.t[l][blockIdx.y] + g[0] * C);
+  const long long n4 = g[1] * C / 4;
+  for (long long i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// The activation tensors of the current plan, carved out of the decoder's buffer.
+void carve(pt_b200_decoder *d) {
+  const Plan &p = d->plan;
   const size_t r0 = (size_t)p.R[0], r1 = (size_t)p.R[1], r2 = (size_t)p.R[2];
-  const size_t need_f = r0 * 192 + r0 * 512 + 7 * r1 * 256 + 7 * r2 * 128 + r2 * 80 + 64 * 24;
-  if (need_f * 4 > d->act_bytes) {
-    if (d->act) cudaFree(d->act);
-    d->act = nullptr;
-    d->act_bytes = 0;
-    PTB_CUDA(cudaMalloc(&d->act, need_f * 4));
-    d->act_bytes = need_f * 4;
-  }
   float *q = static_cast<float *>(d->act);
   auto take = [&](size_t n) {
     float *r = q;
@@ -251,10 +282,97 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
   d->XT[1] = take(r2 * 128); d->H[1] = take(r2 * 128); d->ACC[1] = take(r2 * 128);
   d->P = take(r2 * 128);
   d->POST = take(r2 * 80);
-  PTB_CUDA(cudaMemsetAsync(d->act, 0, (size_t)(reinterpret_cast<char *>(q) - static_cast<char *>(d->act)),
-                           st));
-  // (a copy from pageable memory returns once the source is staged: `host` may go)
-  d->have_plan = true;
+}
+
+size_t act_floats(const Plan &p) {
+  const size_t r0 = (size_t)p.R[0], r1 = (size_t)p.R[1], r2 = (size_t)p.R[2];
+  return r0 * 192 + r0 * 512 + 7 * r1 * 256 + 7 * r2 * 128 + r2 * 80 + 64 * 24;
+}
+
+// Forget every captured decode graph (they hold the activation buffers' old addresses).
+void drop_graphs(pt_b200_decoder *d) {
+  for (int i = 0; i < pt_b200_decoder::kGraphs; ++i) {
+    if (d->gexec[i]) cudaGraphExecDestroy(d->gexec[i]);
+    d->gexec[i] = nullptr;
+    d->g_key[i] = pt_b200_decoder::GKey{};
+    d->g_seen[i] = pt_b200_decoder::GKey{};
+  }
+}
+
+// Make the layout of these requests the current plan: the current one if it matches, a spare
+// one that matches (no rebuild), or a new one built into the buffers of the least recently used
+// spare plan once that plan's last decode has finished.  Then make sure the activation buffers
+// hold this plan's tensors and read zeros in its gap rows (rows another layout used for data are
+// cleared on every switch).  Everything is enqueued on `st`, so later work there is ordered
+// after it.
+int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_window *w) {
+  if (!(d->have_plan && same_windows(d->plan.W, nreq, w))) {
+    if (check_windows(nreq, w)) return -1;
+    int hit = -1;
+    for (int i = 0; i < (int)d->spare.size() && hit < 0; ++i)
+      if (same_windows(d->spare[i].W, nreq, w)) hit = i;
+    Plan next;
+    if (hit >= 0) {
+      next = std::move(d->spare[(size_t)hit]);
+      d->spare.erase(d->spare.begin() + hit);
+    } else {
+      if ((int)d->spare.size() >= pt_b200_decoder::kSparePlans) {
+        Plan old = std::move(d->spare.back());
+        d->spare.pop_back();
+        if (old.used) PTB_CUDA(cudaEventSynchronize(old.used));
+        next.table_block = old.table_block;
+        next.host_stage = old.host_stage;
+        next.table_cap = old.table_cap;
+        next.used = old.used;
+      }
+      if (!next.used) PTB_CUDA(cudaEventCreateWithFlags(&next.used, cudaEventDisableTiming));
+      next.id = ++d->plan_id;
+      if (build_layout(next, st, nreq, w)) {
+        free_plan(next);
+        return -1;
+      }
+    }
+    if (d->have_plan) d->spare.insert(d->spare.begin(), std::move(d->plan));
+    d->plan = std::move(next);
+    d->have_plan = true;
+    const size_t need = act_floats(d->plan) * 4;
+    if (need > d->act_bytes) {
+      // grow (with headroom) once every decode that used the old buffers has finished
+      if (d->done) PTB_CUDA(cudaEventSynchronize(d->done));
+      PTB_CUDA(cudaDeviceSynchronize());
+      drop_graphs(d);
+      if (d->act) cudaFree(d->act);
+      d->act = nullptr;
+      d->act_bytes = 0;
+      // half again as much: batches of the same workload vary by tens of percent, and each
+      // growth waits for the device and drops the captured graphs
+      const size_t cap = need + need / 2;
+      PTB_CUDA(cudaMalloc(&d->act, cap));
+      PTB_CUDA(cudaMemsetAsync(d->act, 0, cap, st));
+      d->act_bytes = cap;
+      d->act_plan = d->plan.id;
+    }
+    carve(d);
+  }
+  if (d->act_plan != d->plan.id) {
+    const Plan &p = d->plan;
+    GapTargets tg{};
+    float *l0[] = {d->Z, d->X0};
+    const int c0[] = {192, 512};
+    float *l1[] = {d->U[0], d->LU[0], d->XB[0], d->XT[0], d->H[0], d->ACC[0], d->OUT1};
+    float *l2[] = {d->U[1], d->LU[1], d->XB[1], d->XT[1], d->H[1], d->ACC[1], d->P, d->POST};
+    tg.nt[0] = 2;
+    tg.nt[1] = 7;
+    tg.nt[2] = 8;
+    for (int i = 0; i < 2; ++i) tg.t[0][i] = l0[i], tg.c[0][i] = c0[i];
+    for (int i = 0; i < 7; ++i) tg.t[1][i] = l1[i], tg.c[1][i] = 256;
+    for (int i = 0; i < 8; ++i) tg.t[2][i] = l2[i], tg.c[2][i] = i == 7 ? 80 : 128;
+    const int nrange = (int)p.T.size() + 1;
+    zero_gaps_kernel<<<dim3((unsigned)(3 * nrange), 8), 256, 0, st>>>(p.gap, nrange, tg);
+    PTB_CUDA(cudaGetLastError());
+    count_launch();
+    d->act_plan = p.id;
+  }
   return 0;
 }
 
@@ -534,7 +652,8 @@ void pt_b200_decoder_destroy(pt_b200_decoder *d) {
   fl(d->post);
   if (d->pqmf) cudaFree(d->pqmf);
   if (d->act) cudaFree(d->act);
-  if (d->plan.table_block) cudaFree(d->plan.table_block);
+  free_plan(d->plan);
+  for (auto &p : d->spare) free_plan(p);
   if (d->zbuf) cudaFree(d->zbuf);
   if (d->wavbuf) cudaFree(d->wavbuf);
   if (d->gerr) cudaFree(d->gerr);
@@ -571,7 +690,7 @@ int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n, const pt_b20
   cudaStream_t st = stream ? (cudaStream_t)stream : d->stream;
   if (build_plan(d, st, n, w)) return -1;
   if (d->graph_on < 0) d->graph_on = getenv("PT_B200_GRAPH") ? atoi(getenv("PT_B200_GRAPH")) : 1;
-  const pt_b200_decoder::GKey key{d->plan_id, z_dev, wav_dev, st, d->prof};
+  const pt_b200_decoder::GKey key{d->plan.id, z_dev, wav_dev, st, d->prof};
   constexpr int NG = pt_b200_decoder::kGraphs;
   int hit = -1;
   bool seen = false;
@@ -613,6 +732,7 @@ int pt_b200_decode_windows(pt_b200_decoder *d, void *stream, int n, const pt_b20
     d->g_seen_next = (d->g_seen_next + 1) % NG;
     if (run_decoder(d, st, z_dev, wav_dev)) return -1;
   }
+  PTB_CUDA(cudaEventRecord(d->plan.used, st));
   PTB_CUDA(cudaEventRecord(d->done, st));
   return 0;
 }
@@ -905,7 +1025,8 @@ int pt_b200_decoder_checkpoints(pt_b200_decoder *d, const float *z_host, int64_t
     d->ck_dev = ck;
     if (run_decoder(d, st, zd, wd)) break;
     d->ck_dev = nullptr;
-    if (cudaEventRecord(d->done, st) != cudaSuccess) break;
+    if (cudaEventRecord(d->plan.used, st) != cudaSuccess || cudaEventRecord(d->done, st) != cudaSuccess)
+      break;
     if (cudaMemcpyAsync(wav_host, wd, (size_t)T * 256 * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
       break;
     bool ok = true;

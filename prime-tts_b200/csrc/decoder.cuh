@@ -69,13 +69,20 @@ struct Plan {
   int *ob01 = nullptr, *ob12 = nullptr;
   long long *zoff = nullptr, *zld = nullptr, *Td = nullptr, *a0 = nullptr;
   long long *row0 = nullptr, *tp = nullptr, *wav0 = nullptr, *klo = nullptr, *khi = nullptr;
-  void *table_block = nullptr;
-  size_t table_bytes = 0;
+  long long *gap = nullptr;        // per level l: nreq + 1 gap-row ranges {first row, rows}
+  void *table_block = nullptr;     // device tables (reused by later plans: table_cap bytes)
+  void *host_stage = nullptr;      // pinned host copy the tables are uploaded from (table_cap)
+  size_t table_bytes = 0, table_cap = 0;
+  uint64_t id = 0;                 // unique per layout (graph keys, gap-row bookkeeping)
+  cudaEvent_t used = nullptr;      // recorded after each decode that read the device tables
 };
 
-// Lay the requests out and upload the tables (masks, convT row maps, per-request tables) on
-// `st`; frees nothing (the caller owns p.table_block).
+// Lay the requests out and upload the tables (masks, convT row maps, per-request tables, gap
+// ranges) on `st`, asynchronously from p.host_stage.  Reuses p.table_block / p.host_stage when
+// they are large enough (the caller makes sure no earlier upload or decode still uses them).
 int build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_window *w);
+// Free a plan's device tables, staging buffer and event.
+void free_plan(Plan &p);
 
 // one conv layer over the rows of a level (all of them, or the tile list {first row, rows})
 int run_conv(pt_b200_decoder *d, cudaStream_t st, const DLayer &L, const float *act, int64_t rows,
@@ -101,6 +108,12 @@ struct pt_b200_decoder {
   std::mutex mu;
   ptb::dec::Plan plan;
   bool have_plan = false;
+  // recently used layouts with their device tables, most recent first: a batch seen again (or
+  // pipelined batches that alternate) switches back without rebuilding, and a new batch reuses the
+  // least recently used plan's buffers instead of allocating
+  static constexpr int kSparePlans = 4;
+  std::vector<ptb::dec::Plan> spare;
+  uint64_t act_plan = ~0ull;    // plan whose gap rows are zero in the activation buffers
   cudaEvent_t done = nullptr;   // recorded after every decode: plan changes wait for it
   uint64_t plan_id = 0;         // bumped whenever the plan (tables, buffers) changes
   // CUDA graphs of the whole decode: captured on the second identical call (same plan, latents,

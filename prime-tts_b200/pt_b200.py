@@ -156,6 +156,8 @@ _SIGS = {
     "pt_b200_ptk_decoder_weights": ([C.c_void_p, C.POINTER(DecWeightsC)], C.c_int),
     "pt_b200_ptk_close": ([C.c_void_p], None),
     "pt_b200_decoder_create_from_ptk": ([C.c_int, C.c_char_p], C.c_void_p),
+    "pt_b200_mma_rate": ([C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                          C.POINTER(C.c_double)], C.c_int),
     "pt_b200_last_error": ([], C.c_char_p),
     "pt_b200_kernel_launches": ([C.c_int], C.c_long),
 }
@@ -191,6 +193,15 @@ def _check(rc: int, what: str) -> None:
 def _p(a: np.ndarray):
     assert a.dtype == np.float32 and a.flags.c_contiguous, (a.dtype, a.flags)
     return a.ctypes.data_as(_f)
+
+
+def mma_rate(device: int = 0, iters: int = 20000) -> dict:
+    """The tensor core's kind::tf32 rate measured live (pt_b200_mma_rate): FLOP per SM clock,
+    aggregate TFLOP/s and the SM clock (MHz) of the run."""
+    f, t, m = C.c_double(), C.c_double(), C.c_double()
+    _check(lib().pt_b200_mma_rate(device, iters, C.byref(f), C.byref(t), C.byref(m)),
+           "pt_b200_mma_rate")
+    return {"flop_per_clk_sm": f.value, "tflops": t.value, "sm_mhz": m.value}
 
 
 def kernel_launches(reset: bool = False) -> int:

@@ -70,3 +70,57 @@ def fp16_rounded(w):
     r.rb_w1 = [[f(a) for a in row] for row in w.rb_w1]
     r.rb_w2 = [[f(a) for a in row] for row in w.rb_w2]
     return r
+
+
+def _tail_tables():
+    """Hann window, window-sum kernel (graph constants 4009 / 3617, from the oracle, which holds
+    the values spec/v21_layers.json records) and the [9,16] cos / sin tables of the irfft bases
+    (graph constants 3607 / 3612, not recorded by the spec: round_fp32(cos / sin(2 pi k n / 16)))."""
+    import ctypes as C
+    import oracle
+    lib = C.CDLL(oracle.LIB_ORACLE)
+    win, win2 = np.zeros(16, np.float32), np.zeros(16, np.float32)
+    f = C.POINTER(C.c_float)
+    lib.or_tail_constants(win.ctypes.data_as(f), win2.ctypes.data_as(f), None, None)
+    k = np.arange(9, dtype=np.float64)[:, None]
+    n = np.arange(16, dtype=np.float64)[None, :]
+    ang = 2.0 * np.pi * k * n / 16.0
+    return win, win2, np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def decoder_range_tensors(w):
+    """Every container record the reference interpreter reads when it runs the decoder's node
+    range (conv_pre .. the PQMF conv) and the constant-only nodes that build its irfft bases and
+    zero-stuff kernel: the decoder records of `decoder_tensors`, the packed kernels of the three
+    tail ConvTranspose nodes, the graph constants (values as spec/v21_layers.json records them;
+    the PQMF filter is `w.pqmf`), and the `dtype.table` record (payload item size of every record,
+    record order) that pt_v21_open requires (runtime/v21/src/pt_v21_host.c:1124-1147)."""
+    import sys, os
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(os.path.dirname(here), "prime-tts_b200"))
+    import pt_b200
+    win, win2, cos9, sin9 = _tail_tables()
+    eye = np.zeros((16, 1, 16), np.float32)
+    for i in range(16):
+        eye[i, 0, i] = 1.0                        # overlap-add kernel, ONNX [Cin][Cout][K]
+    stuff = np.zeros((4, 4, 4), np.float32)
+    for i in range(4):
+        stuff[i, i, 0] = 4.0                      # x4 zero-stuff with gain 4
+    t = decoder_tensors(w)
+    t += [("dec.ConvTranspose.wp", pt_b200.pack_convT(eye, 4)), ("dec.ConvTranspose.b", np.zeros(1, np.float32)),
+          ("dec.ConvTranspose_1.wp", pt_b200.pack_convT(win2.reshape(1, 1, 16), 4)),
+          ("dec.ConvTranspose_1.b", np.zeros(1, np.float32)),
+          ("dec.ConvTranspose_2.wp", pt_b200.pack_convT(stuff, 4)),
+          ("dec.ConvTranspose_2.b", np.zeros(4, np.float32))]
+    sc = lambda v: np.array(v, np.float32)
+    t += [("const.3530", np.full((9, 1), 2.0, np.float32)), ("const.3531", sc(1.0)),
+          ("const.3607", cos9), ("const.3609", sc(16.0)), ("const.3612", sin9),
+          ("const.3614", sc(16.0)), ("const.3616", eye), ("const.3617", win2.reshape(1, 1, 16)),
+          ("const.3618", np.zeros((4, 4, 4), np.float32)), ("const.3867", sc(3.0)),
+          ("const.3916", sc(3.0)), ("const.3970", sc(np.float32(np.pi))),
+          ("const.4009", win.reshape(1, 16, 1)), ("const.4020", sc(1e-9)),
+          ("const.4044", sc(4.0)), ("const.4062", sc(0.0)),
+          ("const.4064", np.asarray(w.pqmf, np.float32).reshape(1, 4, 63))]
+    sizes = [2.0 if name.endswith("#h") else 4.0 for name, _ in t] + [4.0]
+    t.append(("dtype.table", np.array(sizes, np.float32)))
+    return t

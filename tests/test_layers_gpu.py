@@ -10,8 +10,10 @@ pt_v21.h:204-206) and every waveform by SNDR >= 60 dB (:440-447, 505).  Here:
   epilogue (bias, LeakyRelu, residual add, branch sum, /3, the reflection-pad row) and the TF32
   rounding of the stored conv inputs.  Gate: max_rel <= 1e-3 (north-star per-op bound).
 * accumulated: the same checkpoints against the oracle's own full decode (the reference's style of
-  node gate: every upstream difference included).  Gate: the reference's per-node bound for its
-  decoder group, 2e-3 (tests/v21_reference.py:497-498).
+  node gate: every upstream difference included).  Gate: 1e-3 as well -- tighter than the
+  reference's own per-node bound for its decoder group, 2e-3 (tests/v21_reference.py:497-498).
+  The kernels are deterministic (fixed accumulation order, batch-invariant), so these figures are
+  the same on every run.
 * all 64 config-4 requests (the benchmark workload) against the oracle: SNDR >= 60 dB each.
 """
 import os
@@ -26,7 +28,7 @@ import pt_b200
 pytestmark = pytest.mark.gpu
 
 PER_OP_GATE = 1e-3
-ACCUMULATED_GATE = 2e-3
+ACCUMULATED_GATE = 1e-3
 LR, LR_FINAL = np.float32(0.1), np.float32(0.01)
 
 
