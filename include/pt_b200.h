@@ -341,16 +341,23 @@ PT_B200_API int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstr
  * the decoder on overlapping windows (pt_v21_stream_chunk, runtime/v21/src/pt_v21_host.c:
  * 2749-2912) where the windows were meant to cover the receptive field.
  *
- * A session holds the activations of its streams from their first frame: about 205 KB of
- * device memory per latent frame of capacity (sum of T).  Latents are concatenated as for
- * pt_b200_decode_batch_device ([192][T[i]] per stream); pass k reads only its own frames, so
- * z_dev may be filled as frames arrive.  Output samples go to wav_dev at the stream's offset in
- * the concatenated waveform (256*T[i] samples per stream). */
+ * A session's activations are bounded per stream, not per frame: each stream keeps, per
+ * resolution, a fixed window of rows (the rows a pass computes, the receptive context later
+ * passes still read, and its last pass's flush), and before a pass the rows still needed move to
+ * the front of the window; only the per-pass tables (a few KB per stream and pass) grow with the
+ * stream length.  pt_b200_carry_device_bytes tells the size before opening.  Latents are
+ * concatenated as for pt_b200_decode_batch_device ([192][T[i]] per stream); pass k reads only its
+ * own frames, so z_dev may be filled as frames arrive.  Output samples go to wav_dev at the
+ * stream's offset in the concatenated waveform (256*T[i] samples per stream). */
 typedef struct pt_b200_carry pt_b200_carry;
 /* Plan the passes and allocate the session on the decoder's device; NULL on error. */
 PT_B200_API pt_b200_carry *pt_b200_carry_open(pt_b200_decoder *d, int nstreams, const int64_t *T,
                                              int chunk);
 PT_B200_API int pt_b200_carry_passes(const pt_b200_carry *c);
+/* Device bytes the session holds (activation windows, pass tables). */
+PT_B200_API int64_t pt_b200_carry_bytes(const pt_b200_carry *c);
+/* Device bytes a session of these streams would hold (no GPU needed); -1 on bad arguments. */
+PT_B200_API int64_t pt_b200_carry_device_bytes(int nstreams, const int64_t *T, int chunk);
 /* Pass `pass` (0, 1, ... in order, each once) on `stream` (NULL: the decoder's stream),
  * asynchronous; the status covers argument and launch errors (pt_b200_decoder_sync reports
  * device errors). */

@@ -138,6 +138,8 @@ _SIGS = {
                                C.c_int, C.c_int, _i64, C.c_void_p], C.c_int),
     "pt_b200_carry_open": ([C.c_void_p, C.c_int, _i64p, C.c_int], C.c_void_p),
     "pt_b200_carry_passes": ([C.c_void_p], C.c_int),
+    "pt_b200_carry_bytes": ([C.c_void_p], _i64),
+    "pt_b200_carry_device_bytes": ([C.c_int, _i64p, C.c_int], _i64),
     "pt_b200_carry_run": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
     "pt_b200_carry_reset": ([C.c_void_p], C.c_int),
     "pt_b200_carry_close": ([C.c_void_p], None),
@@ -506,6 +508,15 @@ def carry_plan(T, chunk: int = STREAM_WIN - 2 * STREAM_CTX):
     return int(n), lo, hi
 
 
+def carry_device_bytes(T, chunk: int = STREAM_WIN - 2 * STREAM_CTX) -> int:
+    """Device bytes a carried session of these streams holds (pt_b200_carry_device_bytes)."""
+    T = np.ascontiguousarray(T, np.int64)
+    b = lib().pt_b200_carry_device_bytes(len(T), T.ctypes.data_as(_i64p), chunk)
+    if b < 0:
+        _check(-1, "pt_b200_carry_device_bytes")
+    return int(b)
+
+
 class CarrySession:
     """A carried-state streaming session (pt_b200_carry_*): pass k feeds latent frames
     [k*chunk, (k+1)*chunk) of every stream and emits the samples whose inputs are complete."""
@@ -517,6 +528,7 @@ class CarrySession:
         if not self.h:
             _check(-1, "pt_b200_carry_open")
         self.passes = lib().pt_b200_carry_passes(self.h)
+        self.bytes = int(lib().pt_b200_carry_bytes(self.h))
 
     def run(self, k: int, z_dev: int, wav_dev: int, stream=None) -> None:
         _check(lib().pt_b200_carry_run(self.h, stream, k, z_dev, wav_dev), "pt_b200_carry_run")

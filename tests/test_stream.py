@@ -145,8 +145,26 @@ def test_carry_plan_rejects_bad_arguments():
 
 def test_carry_plan_rejects_sessions_past_the_32_bit_row_limit():
     """Epilogue offsets are 32-bit: a session whose level-2 tensors would pass 2^31 elements is
-    refused by the planner with a message, before any device memory is touched."""
-    T = np.full(2000, 600, np.int64)   # 1.2M frames: ~19M level-2 rows x 128 channels
+    refused by the planner with a message, before any device memory is touched.  The tensors hold
+    a bounded window per stream, so the limit is a stream count, not a frame count."""
+    T = np.full(2000, 600, np.int64)   # 1.2M frames: accepted, the windows are per stream
+    assert pt_b200.lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(pt_b200._i64p), 32, None,
+                                            None, 0) == 19
+    T = np.full(14000, 600, np.int64)  # ~19M level-2 window rows x 128 channels
     n = pt_b200.lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(pt_b200._i64p), 32, None, None, 0)
     assert n == -1
     assert b"too large" in pt_b200.lib().pt_b200_last_error()
+
+
+def test_carried_session_memory_is_bounded_per_stream():
+    """A session's activations grow with the number of streams, not with their length: each
+    stream keeps a fixed window of rows per resolution (pt_b200_carry_device_bytes); only the
+    per-pass tables (a few KB per stream and pass) grow with the number of passes."""
+    short = pt_b200.carry_device_bytes([400] * 8, 32)
+    long = pt_b200.carry_device_bytes([4000] * 8, 32)   # 10 x the frames, 10 x the passes
+    assert long < 1.5 * short, (short, long)
+    assert pt_b200.carry_device_bytes([400] * 16, 32) > 1.8 * short
+    T, _ = pt_b200.config5()
+    b = pt_b200.carry_device_bytes(T, 32)
+    print(f"\nconfig 5 carried session: {b / 1e9:.2f} GB for {len(T)} streams, {sum(T)} frames")
+    assert b < 12e9, b
