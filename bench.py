@@ -183,7 +183,7 @@ def config_dict(n_gpus, T, kind="batch", scheme="carry"):
 
 # ----------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the timed region runs.
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the timed regions run.
     start() returns once the first sample has arrived (nvidia-smi takes a moment to start), so
     the samples cover the timed region rather than the tool's start-up."""
 
@@ -296,14 +296,22 @@ LAYER_NAMES = (["stage", "conv_pre", "ups.0"]
                + ["conv_post", "tail"])
 
 
-def layer_table(recs, steps):
+def layer_table(recs, steps, mma=None):
     """Markdown table of one decode's launches averaged over `steps` decodes: time, algorithmic
     TFLOP/s and GB/s, and which roofline bounds the layer (FLOP/B against the ridge point of the
-    measured TF32 and HBM peaks)."""
+    TF32 and HBM peaks).  The TF32 peak is the live tcgen05 kind::tf32 probe (`mma`: the tensor
+    pipe's own rate at the clock a tensor-saturating load holds) when given, else the measured
+    cuBLAS bf16 burst rate / 2."""
     peaks, src = measured_peaks()
-    tf = peaks["bf16_tflops_sustained"] / 2.0 * 1e12
+    if mma:
+        tf = mma["tflops"] * 1e12
+        tsrc = (f"live kind::tf32 probe {mma['flop_per_clk_sm']:.0f} FLOP/clk/SM at "
+                f"{mma['sm_mhz']:.0f} MHz")
+    else:
+        tf = peaks["bf16_tflops"] / 2.0 * 1e12
+        tsrc = f"{src} bf16_tflops / 2"
     bw = peaks["hbm_gbs"] * 1e9
-    lines = [f"peaks ({src}): TF32 {tf / 1e12:.1f} TFLOP/s, HBM {bw / 1e9:.0f} GB/s, "
+    lines = [f"peaks: TF32 {tf / 1e12:.1f} TFLOP/s ({tsrc}), HBM {bw / 1e9:.0f} GB/s ({src}), "
              f"ridge {tf / bw:.0f} FLOP/B",
              "| layer | kernel | us | TFLOP/s | GB/s | FLOP/B | bound | roofline us | of roofline |",
              "|---|---|---:|---:|---:|---:|---|---:|---:|"]
@@ -513,7 +521,7 @@ def main():
                 lt = dec.launch_times()
                 acc = lt if acc is None else [(a[0], a[1], a[2] + b[2], a[3], a[4])
                                               for a, b in zip(acc, lt)]
-        print(layer_table(acc, max(args.steps, 1)))
+        print(layer_table(acc, max(args.steps, 1), pt_b200.mma_rate(local)))
         dec.close()
         return 0
 
@@ -567,7 +575,6 @@ def main():
     gpu_launches = pt_b200.kernel_launches()
     barrier()
     dec.profile(False)
-    clk = clocks.stop(list(range(world))) if rank == 0 else None
     per_rank = gather_ranks([rank, len(T), int(T.sum()), total_ms / args.steps])
     t_step = max(r[3] for r in per_rank) / 1e3
 
@@ -653,6 +660,9 @@ def main():
                         "batches": args.steps,
                         "mode": "pipelined like `value`, a different config-4 draw every step "
                                 "(seeds 3 + 10k): plan building and eager launches timed"}
+    # the sampler ran over the device-timed steps and every host-buffer timed region after them
+    # (one device region alone is ~0.1 s: a single 100 ms sample)
+    clk = clocks.stop(list(range(world))) if rank == 0 else None
     ok = np.isfinite(wav_host.numpy()).all()
 
     # ---- config 5 alongside the batch workload (carried-state streaming, per-rank shards) -----
