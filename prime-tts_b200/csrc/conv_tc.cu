@@ -205,6 +205,9 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   ConvGeom g = L.g;
   const long long mtl = (L.g.n_cols + kBM - 1) / kBM;
   g.tile_rows = kTNRows;
+  // three activation windows for kernel-3 convs (a window lasts three taps), else two windows
+  // and a third weight stage; residual instances always run two windows
+  g.win_slots = TNCfg<F>::kRes || L.g.ntap > 3 ? 2 : 3;
   if (!L.g.tiles) {
     // The tile height whose last wave is fullest: waves x (rows + a per-tile cost of 16 rows,
     // the weight stream and pipeline fill) over heights 256 .. 160.

@@ -54,6 +54,7 @@ struct ConvGeom {
   // Channels-on-M kernel only: rows per tile of the uniform schedule (a multiple of 16, <= 256;
   // 0 = 256), chosen by the launcher so that the last wave of tiles is nearly full.
   int tile_rows;
+  int win_slots;   // channels-on-M kernel: activation windows in its shared-memory ring (2 or 3)
 };
 
 struct EpiParams {
@@ -575,39 +576,44 @@ constexpr int kTNRows = 256;    // time rows per tile (MMA N)
 // allocator + MMA issuer, E+2 weight producer.
 
 // Pipeline shape.  Windows and weight stages come from two producer warps, so each ring runs
-// ahead of the MMAs by its own depth: a k = 3 layer consumes a 32-channel window in three weight
-// stages (~0.8 us of MMA), less than one window's DRAM latency plus transfer, and needs windows
-// two chunks ahead whatever the weight ring holds.  With one producer issuing both in order, the
-// weight ring capped the window lead at about one chunk.  On config 4: 5,445 -> 5,327 us per
-// decode summed over the layers (256-channel k3 convs2 94 -> 84 us); three window slots with four
-// weight stages beat two with seven (5,357) and four with two (6,428, weight-starved).
-#ifndef PTB_TN_WIN_SLOTS
-#define PTB_TN_WIN_SLOTS 3
-#endif
-#ifndef PTB_TN_A_STAGES
-#define PTB_TN_A_STAGES 4
+// ahead of the MMAs by its own depth.  Weight stages hold PTB_TN_GROUP consecutive (chunk, tap)
+// steps of 16 KiB each, so the MMA issuer waits on one barrier and commits one release per
+// 4 x PTB_TN_GROUP MMAs: the tensor pipe runs at most about one M128 x N256 MMA (~128 cycles)
+// ahead of its issuing thread, and with the epilogue warps sharing the SM sub-partitions every
+// handshake between two MMAs risks an idle pipe (32 KiB stages: 4,829 -> 4,722 us per config-4
+// decode, mostly on the residual-reading k = 7 / 11 layers).  One shared-memory ring holds the
+// activation windows and the weight stages, split per launch: kernel-3 layers consume a
+// 32-channel window in 3 taps (~1.3 us of MMA, less than a window's load) and take three windows
+// and two weight stages; wider kernels hold a window for 7-11 taps and take two windows and
+// three weight stages (k = 3 convs1 61.6 vs 63.5 us, k = 11 convs1 139.5 vs 148.4 us, either way
+// round losing).
+#ifndef PTB_TN_GROUP
+#define PTB_TN_GROUP 2
 #endif
 // Residual-reading instances (two staged outputs, 4 KB of staging per warp) run 12 epilogue warps
-// and give up the third window slot for their staging: 5,040 -> 4,962 us per config-4 decode
-// (256-channel k3 convs2 82 -> 79 us, 128-channel k3 convs2 131 -> 121 us).  Three weight stages
-// instead of two window slots lose on the tensor-bound k7 / k11 convs2 layers (5,140).
+// and keep two windows and three weight stages whatever the kernel size.
 #ifndef PTB_RES_EW
 #define PTB_RES_EW 12
-#endif
-#ifndef PTB_RES_WS
-#define PTB_RES_WS 2
-#endif
-#ifndef PTB_RES_AS
-#define PTB_RES_AS PTB_TN_A_STAGES
 #endif
 template <int F>
 struct TNCfg {
   static constexpr bool kRes = F != EF_GENERIC && (F & EF_RES);
-  static constexpr int kWinSlots = kRes ? PTB_RES_WS : PTB_TN_WIN_SLOTS;
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
-  static constexpr int kAStages = kRes ? PTB_RES_AS : PTB_TN_A_STAGES;
+  static constexpr int kGroup = PTB_TN_GROUP;                     // weight tiles per stage
+  static constexpr int kAS = kA * kGroup;                         // bytes per weight stage
+  // ring of windows + weight stages: (3 windows, 2 stages) or (2, 3); residual instances (2, 3)
+  static constexpr int kWinMax = kRes ? 2 : 3;                    // barrier slots
+  static constexpr int kStageMax = 3;
+  static constexpr int kRing = kRes ? 2 * kWinBytes + 3 * kAS
+                                    : (3 * kWinBytes + 2 * kAS > 2 * kWinBytes + 3 * kAS
+                                           ? 3 * kWinBytes + 2 * kAS
+                                           : 2 * kWinBytes + 3 * kAS);
+  // weight stages that fit beside `ws` windows
+  __host__ __device__ static constexpr int stages(int ws) {
+    return (kRing - ws * kWinBytes) / kAS < kStageMax ? (kRing - ws * kWinBytes) / kAS : kStageMax;
+  }
   // Single-output instances without residual or branch-sum inputs (conv_pre, convs1, conv_post)
   // run 16 epilogue warps of one staging slot each: their epilogue is a chain of short dependent
   // steps per 16-row pass, and on the 128-channel k = 3 layers it, not the MMA, sets the pace;
@@ -617,7 +623,7 @@ struct TNCfg {
   static constexpr int kSlots = kEpiWarps == 16 ? 1 : 2;          // staging slots per warp
   static constexpr int kStageWarp = kSlots * 16 * kBK * 4;        // slots x (16 rows x 32 channels)
   static constexpr int kStage = kEpiWarps * kStageWarp;           // 32 KiB (48 KiB at 12 warps)
-  static constexpr int kBytes = kWinSlots * kWinBytes + kAStages * kA + kStage + 1024 + 256;
+  static constexpr int kBytes = kRing + kStage + 1024 + 256;
   static_assert(kBytes <= 227 * 1024, "TN kernel shared memory over the per-CTA limit");
 };
 
@@ -891,25 +897,29 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
                       const __grid_constant__ CUtensorMap tmO1, const ConvGeom g, const EpiParams e,
                       uint32_t *gerr) {
   using P = TNCfg<F>;
-  constexpr int AS = P::kAStages;
-  constexpr int WS = P::kWinSlots;
+  constexpr int WSM = P::kWinMax, ASM = P::kStageMax;   // barrier slots
+  const int WS = g.win_slots, AS = P::stages(g.win_slots);   // this launch's ring split
   constexpr int EW = P::kEpiWarps;   // epilogue warps; then the window producer, MMA, weights
+  if (WS < 2 || WS > WSM || AS < 1) {   // uniform over the grid: nothing has started yet
+    if (threadIdx.x == 0) atomicOr(gerr, ERR_BAD_ARGS);
+    return;
+  }
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
   const uint32_t win0 = base, ast0 = base + WS * P::kWinBytes;
-  const uint32_t stg0 = ast0 + AS * P::kA;   // epilogue output staging, kStageWarp per warp
+  const uint32_t stg0 = base + P::kRing;   // epilogue output staging, kStageWarp per warp
   const uint32_t bar0 = stg0 + P::kStage;
   auto wfull = [&](int s) { return bar0 + 8u * s; };
-  auto wempty = [&](int s) { return bar0 + 8u * (WS + s); };
-  auto afull = [&](int s) { return bar0 + 8u * (2 * WS + s); };       // accumulator ready
-  auto aempty = [&](int s) { return bar0 + 8u * (2 * WS + 2 + s); };  // accumulator drained
-  auto sfull = [&](int s) { return bar0 + 8u * (2 * WS + 4 + s); };   // weight stage loaded
-  auto sempty = [&](int s) { return bar0 + 8u * (2 * WS + 4 + AS + s); };
-  const uint32_t dbar = bar0 + 8u * (2 * WS + 4 + 2 * AS);
+  auto wempty = [&](int s) { return bar0 + 8u * (WSM + s); };
+  auto afull = [&](int s) { return bar0 + 8u * (2 * WSM + s); };       // accumulator ready
+  auto aempty = [&](int s) { return bar0 + 8u * (2 * WSM + 2 + s); };  // accumulator drained
+  auto sfull = [&](int s) { return bar0 + 8u * (2 * WSM + 4 + s); };   // weight stage loaded
+  auto sempty = [&](int s) { return bar0 + 8u * (2 * WSM + 4 + ASM + s); };
+  const uint32_t dbar = bar0 + 8u * (2 * WSM + 4 + 2 * ASM);
   uint32_t *tmem_slot =
-      reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (2 * WS + 5 + 2 * AS));
+      reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (2 * WSM + 5 + 2 * ASM));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -955,7 +965,7 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
   if (warp == EW) {
     if (lane == 0) {
       // ---------------- TMA producer: activation windows (one per 32-channel chunk)
-      int wiss[WS] = {};
+      int wiss[WSM] = {};
       bool ok = true;
       int cw = 0;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -987,25 +997,36 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
     }
   } else if (warp == EW + 2) {
     if (lane == 0) {
-      // ---------------- TMA producer: weight stages (one per chunk and tap)
-      int aiss[AS];
+      // ---------------- TMA producer: weight stages, kGroup (chunk, tap) steps each; a tile's
+      // steps run chunk-major, taps fastest, and a stage never spans two tiles
+      constexpr int GR = P::kGroup;
+      int aiss[ASM];
 #pragma unroll
-      for (int s = 0; s < AS; ++s) aiss[s] = 0;
+      for (int s = 0; s < ASM; ++s) aiss[s] = 0;
       bool ok = true;
       int ca = 0;
+      const int steps = kc * g.ntap;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const int mi = tn_tile(g, t, mt, tt, ntiles).mi;
-        for (int c = 0; c < kc && ok; ++c)
-          for (int k = 0; k < g.ntap; ++k, ++ca) {
-            const int as = ca % AS;
-            if (!mbar_wait(sempty(as), ((ca / AS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
-              ok = false;
-              break;
-            }
-            mbar_expect_tx(sfull(as), P::kA);
-            tma_load_2d(ast0 + as * P::kA, &tmW, sfull(as), k * g.cin32 + c * kBK, mi * kBM);
-            ++aiss[as];
+        int c = 0, k = 0;
+        for (int j = 0; j < steps; j += GR, ++ca) {
+          const int as = ca % AS;
+          if (!mbar_wait(sempty(as), ((ca / AS) & 1) ^ 1, abort_flag, gerr, ERR_WAIT_EMPTY)) {
+            ok = false;
+            break;
           }
+          const int nb = steps - j < GR ? steps - j : GR;
+          mbar_expect_tx(sfull(as), nb * P::kA);
+          for (int b = 0; b < nb; ++b) {
+            tma_load_2d(ast0 + as * P::kAS + b * P::kA, &tmW, sfull(as), k * g.cin32 + c * kBK,
+                        mi * kBM);
+            if (++k == g.ntap) {
+              k = 0;
+              ++c;
+            }
+          }
+          ++aiss[as];
+        }
       }
       if (!ok)
         for (int s = 0; s < AS; ++s)
@@ -1043,6 +1064,8 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + ab * kTNRows;
         uint32_t accum = 0;
+        int sub = 0;   // weight tile within the current stage
+        uint64_t dA = dA0 + static_cast<uint64_t>(as * (P::kAS / 16));
         for (int c = 0; c < kc && ok; ++c) {
           if (!mbar_wait(wfull(ws), wph, abort_flag, gerr, ERR_WAIT_FULL)) {
             ok = false;
@@ -1050,21 +1073,28 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
           }
           uint64_t dB = dW0 + static_cast<uint64_t>(ws * (P::kWinBytes / 16));
           for (int k = 0; k < ntap; ++k) {
-            if (!mbar_wait(sfull(as), aph, abort_flag, gerr, ERR_WAIT_FULL)) {
-              ok = false;
-              break;
+            if (sub == 0) {
+              if (!mbar_wait(sfull(as), aph, abort_flag, gerr, ERR_WAIT_FULL)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
             }
-            tc_fence_after();
-            const uint64_t dA = dA0 + static_cast<uint64_t>(as * (P::kA / 16));
             mma_tf32(acc, dA, dB, idesc, accum);
             mma_tf32(acc, dA + 2u, dB + 2u, idesc, 1u);
             mma_tf32(acc, dA + 4u, dB + 4u, idesc, 1u);
             mma_tf32(acc, dA + 6u, dB + 6u, idesc, 1u);
             accum = 1u;
-            mma_commit(sempty(as));
-            if (++as == AS) {
-              as = 0;
-              aph ^= 1u;
+            dA += static_cast<uint64_t>(P::kA / 16);
+            if (++sub == P::kGroup || (c == kc - 1 && k == ntap - 1)) {
+              // the stage's last weight tile (or the tile's last step): release it
+              mma_commit(sempty(as));
+              sub = 0;
+              if (++as == AS) {
+                as = 0;
+                aph ^= 1u;
+              }
+              dA = dA0 + static_cast<uint64_t>(as * (P::kAS / 16));
             }
             dB += static_cast<uint64_t>(dtap);
           }
