@@ -811,8 +811,9 @@ def measure_stream(args, world, rank, local, dec, stream, flush, barrier, gather
     barrier()
     finite = bool(torch.isfinite(wav).all().item())
     passes = sess.passes
+    sess_bytes = sess.bytes
     sess.close()
-    per_rank = gather_ranks([rank, len(T), int(T.sum()), ms / steps, passes])
+    per_rank = gather_ranks([rank, len(T), int(T.sum()), ms / steps, passes, sess_bytes])
     t = max(r[3] for r in per_rank) / 1e3
     audio = audio_seconds(sum(T_all))
     return {"workload": "BASELINE config 5: 512 streams per GPU, T~U{100..1000} (seed 4), 32 new "
@@ -822,7 +823,8 @@ def measure_stream(args, world, rank, local, dec, stream, flush, barrier, gather
             "streams": len(T_all), "frames": int(sum(T_all)), "steps": steps,
             "ms_per_step": round(t * 1e3, 3), "output_finite": finite,
             "ranks": [{"rank": int(r[0]), "streams": int(r[1]), "frames": int(r[2]),
-                       "ms_per_step": round(r[3], 3), "passes": int(r[4])} for r in per_rank]}
+                       "ms_per_step": round(r[3], 3), "passes": int(r[4]),
+                       "session_gb": round(r[5] / 1e9, 3)} for r in per_rank]}
 
 
 if __name__ == "__main__":

@@ -336,19 +336,22 @@ PT_B200_API int pt_b200_stream_decode(pt_b200_decoder *d, void *stream, int nstr
  * frames [k*chunk, (k+1)*chunk) of every stream still running, and every layer computes only
  * the rows whose inputs are now complete, reading the rows it needs from earlier passes out of
  * the session's activations (the carried state).  Each pass emits the output samples whose
- * receptive field is complete (24 latent frames of look-ahead; a stream's last pass flushes
- * it), bit-identical to the whole-utterance decode.  This replaces the reference's re-run of
- * the decoder on overlapping windows (pt_v21_stream_chunk, runtime/v21/src/pt_v21_host.c:
- * 2749-2912) where the windows were meant to cover the receptive field.
+ * receptive field is complete (24 latent frames of look-ahead), bit-identical to the
+ * whole-utterance decode; the pass after the one that brings a stream's last frames (it brings
+ * none of its own) flushes that stream, so a session runs ceil(max T / chunk) + 1 passes.  This
+ * replaces the reference's re-run of the decoder on overlapping windows (pt_v21_stream_chunk,
+ * runtime/v21/src/pt_v21_host.c:2749-2912) where the windows were meant to cover the receptive
+ * field.
  *
  * A session's activations are bounded per stream, not per frame: each stream keeps, per
- * resolution, a fixed window of rows (the rows a pass computes, the receptive context later
- * passes still read, and its last pass's flush), and before a pass the rows still needed move to
- * the front of the window; only the per-pass tables (a few KB per stream and pass) grow with the
- * stream length.  pt_b200_carry_device_bytes tells the size before opening.  Latents are
- * concatenated as for pt_b200_decode_batch_device ([192][T[i]] per stream); pass k reads only its
- * own frames, so z_dev may be filled as frames arrive.  Output samples go to wav_dev at the
- * stream's offset in the concatenated waveform (256*T[i] samples per stream). */
+ * resolution, a fixed window of rows (the rows a pass computes and the receptive context later
+ * passes still read; the flush, in a pass of its own, fits the same window), and before a pass
+ * the rows still needed move to the front of the window; only the per-pass tables (a few KB per
+ * stream and pass) grow with the stream length.  pt_b200_carry_device_bytes tells the size
+ * before opening.  Latents are concatenated as for pt_b200_decode_batch_device ([192][T[i]] per
+ * stream); pass k reads only its own frames, so z_dev may be filled as frames arrive.  Output
+ * samples go to wav_dev at the stream's offset in the concatenated waveform (256*T[i] samples
+ * per stream). */
 typedef struct pt_b200_carry pt_b200_carry;
 /* Plan the passes and allocate the session on the decoder's device; NULL on error. */
 PT_B200_API pt_b200_carry *pt_b200_carry_open(pt_b200_decoder *d, int nstreams, const int64_t *T,

@@ -12,8 +12,9 @@
 // last tile rounds up to 16 rows (the MMA's N step), computing up to 15 rows past it from
 // incomplete inputs; nothing reads those rows before the next pass, whose tiles start at that
 // frontier, rewrites them.  This keeps level 0, where 16 rows are 16 latent frames, from adding to
-// the emission delay.  In a stream's last pass every layer runs to the end of the stream rounded
-// up into the zero rows after it.  The tail then emits the samples whose frames are all complete.
+// the emission delay.  The pass after the one that brings a stream's last frames flushes it:
+// every layer runs to the end of the stream rounded up into the zero rows after it.  The tail
+// then emits the samples whose frames are all complete.
 // Rows are computed once, by the same kernels with the same operand order as the
 // whole-utterance decode, and read back from where earlier passes left them, so the output is
 // bit-identical to it.  The planner does this bookkeeping in virtual rows: each stream laid out
@@ -25,11 +26,12 @@
 // off_{k-1}, a multiple of 16) when the pass would not fit the window otherwise: the rows every
 // later pass may still touch -- the lowest row any launch reads (its tile start minus its reach,
 // minus a 16-row slack) or writes, and the lowest conv_post row the tail reads -- are moved to
-// the front of the window by a block copy, for every tensor of that level.  A stream's last pass
+// the front of the window by a block copy, for every tensor of that level.  A stream's flush pass
 // first clears the 48 rows after its end (its padding: the whole-stream layout's zero gap), since
 // the window reuses rows that held earlier frames.  So a session holds about (chunk + receptive
-// lag + final flush) rows per stream and level instead of the whole stream.  Tile rows, row masks, the upsamplers' row maps and the per-stream
-// staging / tail offsets are tabulated per pass.
+// lag) rows per stream and level instead of the whole stream: at 32-frame chunks windows of 112
+// / 288 / 800 rows at levels 0 / 1 / 2.  Tile rows, row masks, the upsamplers' row maps and the
+// per-stream staging / tail offsets are tabulated per pass.
 //
 // Buffers.  A tensor a later pass still reads must not be overwritten by another layer in
 // between.  Per level the session keeps u, leaky(u), the branch sum and the level's output, and
@@ -114,10 +116,15 @@ int plan_carry(CarryPlan &P, int n, const int64_t *T, int chunk) {
               "rows of stream data); open fewer streams", (long long)P.R[2]);
   int64_t maxT = 0;
   for (int s = 0; s < n; ++s) maxT = std::max(maxT, T[s]);
-  P.npass = (int)((maxT + chunk - 1) / chunk);
+  // a stream's frames arrive in passes 0 .. ceil(T / chunk) - 1, each run like any other; the
+  // pass after them flushes it (every layer to the stream's end).  Flushing in the pass that
+  // brings the last frames would make that pass span the receptive lag, the last chunk and the
+  // flush at once, and the windows are sized by the largest pass: level-2 windows of 1,312 rows
+  // instead of 768 at 32-frame chunks.
+  P.npass = (int)((maxT + chunk - 1) / chunk) + 1;
   const int np = P.npass;
   P.done.resize(n);
-  for (int s = 0; s < n; ++s) P.done[s] = (int)((T[s] + chunk - 1) / chunk) - 1;
+  for (int s = 0; s < n; ++s) P.done[s] = (int)((T[s] + chunk - 1) / chunk);
 
   // ---- 1. frontiers in virtual rows; per pass and stream, the local rows each level's tensors
   // are touched over [lo, hi) and written up to (wr)
@@ -149,7 +156,7 @@ int plan_carry(CarryPlan &P, int n, const int64_t *T, int chunk) {
       const int64_t Ts = T[s];
       const size_t ks = (size_t)k * n + s;
       const int64_t fz1 = std::min<int64_t>(Ts, (int64_t)(k + 1) * chunk);
-      const bool done = fz1 == Ts;
+      const bool done = k >= P.done[s];
       P.f0.push_back(fz[s]);
       P.f1.push_back(fz1);
       zmax = std::max<long long>(zmax, (fz1 - fz[s] + 31) / 32);

@@ -104,15 +104,17 @@ CARRY_CHUNKS = [1, 7, 32, 64, 1000]
 @pytest.mark.parametrize("chunk", CARRY_CHUNKS)
 def test_carry_plan_emits_every_sample_once_in_order(chunk):
     """Pass after pass, each stream's emitted ranges are contiguous, start at 0, never go back,
-    and the stream's last pass (the one that delivers its last frame) ends at 256 T."""
+    and the stream's flush pass (the one after the pass that delivers its last frame) ends at
+    256 T; the pass delivering the last frame still holds back the look-ahead."""
     n, lo, hi = pt_b200.carry_plan(CASES_T, chunk)
-    assert n == -(-max(CASES_T) // chunk)
+    assert n == -(-max(CASES_T) // chunk) + 1
     for s, T in enumerate(CASES_T):
         assert lo[0, s] == 0
         np.testing.assert_array_equal(lo[1:, s], hi[:-1, s])
         assert (hi[:, s] >= lo[:, s]).all()
-        last = -(-T // chunk) - 1
+        last = -(-T // chunk)
         assert hi[last, s] == 256 * T and (hi[last:, s] == 256 * T).all()
+        assert hi[last - 1, s] < 256 * T
 
 
 @pytest.mark.parametrize("chunk", CARRY_CHUNKS)
@@ -149,8 +151,8 @@ def test_carry_plan_rejects_sessions_past_the_32_bit_row_limit():
     a bounded window per stream, so the limit is a stream count, not a frame count."""
     T = np.full(2000, 600, np.int64)   # 1.2M frames: accepted, the windows are per stream
     assert pt_b200.lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(pt_b200._i64p), 32, None,
-                                            None, 0) == 19
-    T = np.full(14000, 600, np.int64)  # ~19M level-2 window rows x 128 channels
+                                            None, 0) == 20   # 19 with frames + the flush
+    T = np.full(24000, 600, np.int64)  # ~20M level-2 window rows x 128 channels
     n = pt_b200.lib().pt_b200_carry_plan(len(T), T.ctypes.data_as(pt_b200._i64p), 32, None, None, 0)
     assert n == -1
     assert b"too large" in pt_b200.lib().pt_b200_last_error()
@@ -167,4 +169,4 @@ def test_carried_session_memory_is_bounded_per_stream():
     T, _ = pt_b200.config5()
     b = pt_b200.carry_device_bytes(T, 32)
     print(f"\nconfig 5 carried session: {b / 1e9:.2f} GB for {len(T)} streams, {sum(T)} frames")
-    assert b < 12e9, b
+    assert b < 8e9, b
