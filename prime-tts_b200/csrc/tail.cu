@@ -4,15 +4,21 @@
 // Per request the conv_post output holds Tp frames x 72 channels = 4 subbands x (9 log-magnitudes,
 // 9 phase logits).  One CTA produces kTailW consecutive output samples:
 //   1. frames:  mag = exp(a), ph = pi * sin(b), re/im = mag * cos/sin(ph); the 9 -> 16 inverse
-//      real-DFT basis contraction in double (the reference einsum's double accumulation,
-//      runtime/v21/src/pt_v21_host.c:1963-1995), re + im, times the periodic Hann window;
+//      real-DFT basis contraction (the reference einsum, runtime/v21/src/pt_v21_host.c:
+//      1963-1995, accumulates in double; here fp32 fused multiply-adds), re + im, times the
+//      periodic Hann window;
 //   2. overlap-add (hop 4, the eye(16) ConvTranspose) divided by the clipped window-sum
 //      envelope (ConvTranspose_1 of ones with the Hann^2 kernel, Clip 1e-9, Div), trimmed [8:-8];
 //   3. x4 zero-stuffed upsampling with gain 4 (ConvTranspose_2) folded into the 63-tap PQMF
 //      synthesis conv: only taps landing on a stuffed sample (one in four) are evaluated.
-// Every fp32 step keeps the reference's operation order (no FMA contraction), so apart from the
-// exp/sin/cos implementations (and the sign of an exact-zero sample) the tail reproduces the
-// reference bit for bit.
+// The tail is instruction-bound (its HBM bytes are small), so it trades the reference's exact
+// operation order for fewer instructions where the result moves by less than a microunit: the
+// magnitude's exp and the phase rotation's sincos use the hardware approximations (__expf;
+// __sincosf on a phase in [-pi, pi], absolute error below 2^-21), the basis sums run in fp32
+// FMAs and the PQMF taps fuse their multiply-adds; sin(b), whose argument is unbounded, stays
+// the accurate sinf.  Against the reference's own order (the CPU oracle): max relative error
+// 4.3e-7 and >= 132 dB on N(0, 0.25) spectra at Tp = 2 .. 3617 (the test gate: 1e-5, 100 dB);
+// 148 -> 123 us per config-4 decode.
 #include <cmath>
 #include <mutex>
 
@@ -20,7 +26,7 @@
 
 namespace ptb {
 
-constexpr int kTailW = 1024;                 // output samples per CTA (66.5 KB of shared memory)
+constexpr int kTailW = 1024;                 // output samples per CTA (45.8 KB of shared memory)
 // 9 warps: 8 frames x 36 bins in the magnitude / phase phase, the 576 (frame, band, half) basis
 // items of a chunk in two rounds, the 276 staged overlap-add samples in one; the PQMF phase uses 8
 constexpr int kTailThreads = 288;
@@ -29,13 +35,13 @@ constexpr int kTailF = kTailW / 16 + 8;      // staged frames (chunk + halo): NF
 constexpr int kTailM = kTailW / 4 + 20;      // staged trimmed-OLA samples per band
 
 __constant__ float c_win[16], c_win2[16];
-__constant__ double c_bcd[144], c_bsd[144];   // the fp32 basis values, held exactly in double
+__constant__ float c_bc[144], c_bs[144];   // the inverse real-DFT basis (cosine, sine rows)
 
 // Frame rows are 68 floats (4 bands x 16 + 4 pad): the overlap-add reads 8 consecutive frames at
 // one (band, sample) per warp and the stride of 68 puts those reads on 32 distinct banks.
 constexpr int kFrStride = 68;
 struct TailSmem {
-  double re[kTailF][4][9], im[kTailF][4][9];   // per frame, band, bin (converted once)
+  float re[kTailF][4][9], im[kTailF][4][9];   // per frame, band, bin
   float fr[kTailF][kFrStride];                 // windowed frames, [frame][band * 16 + n]
   float4 sm[kTailM];                           // trimmed OLA, 4 bands interleaved
   float4 h[63];                                // PQMF taps, 4 bands interleaved
@@ -56,14 +62,14 @@ struct TailArgs {
 };
 
 // magnitude / phase of one bin: re = exp(a) * cos(pi * sin(b)), im = exp(a) * sin(pi * sin(b))
-// (the cosine and sine of the phase come from one sincos call: one argument reduction).  F32:
-// the fp32 functions; otherwise double-precision ones rounded to fp32 (the reference's choice
-// for small tensors).
+// (the cosine and sine of the phase come from one sincos call).  F32: fp32 functions, the
+// hardware approximations for exp and for the phase's sincos; otherwise double-precision ones
+// rounded to fp32 (the reference's choice for small tensors).
 template <bool F32>
 __device__ __forceinline__ void tr_bin(float la, float lb, float &rv, float &iv) {
   float mag, sb, c, sn;
   if constexpr (F32) {
-    mag = expf(la);
+    mag = __expf(la);
     sb = sinf(lb);
   } else {
     mag = (float)exp((double)la);
@@ -71,7 +77,7 @@ __device__ __forceinline__ void tr_bin(float la, float lb, float &rv, float &iv)
   }
   const float ph = __fmul_rn(sb, 3.1415927410125732f);
   if constexpr (F32) {
-    sincosf(ph, &sn, &c);
+    __sincosf(ph, &sn, &c);
   } else {
     double sd, cd;
     sincos((double)ph, &sd, &cd);
@@ -87,7 +93,7 @@ __device__ __forceinline__ void tr_bin(float la, float lb, float &rv, float &iv)
 template <bool F32>
 __device__ __forceinline__ void bins_loop(const float *pc, long long st_t, long long cst,
                                           long long F0, int NF, int flo, int fhi, int fl0,
-                                          double *pre, double *pim) {
+                                          float *pre, float *pim) {
   auto ld = [&](int f, float &x, float &y) {
     x = 0.0f;
     y = 0.0f;
@@ -109,39 +115,39 @@ __device__ __forceinline__ void bins_loop(const float *pc, long long st_t, long 
     float rv, iv, rv2, iv2;
     tr_bin<F32>(la, lb, rv, iv);
     tr_bin<F32>(la2, lb2, rv2, iv2);
-    pre[fl * 36] = v1 ? (double)rv : 0.0;
-    pim[fl * 36] = v1 ? (double)iv : 0.0;
+    pre[fl * 36] = v1 ? rv : 0.0f;
+    pim[fl * 36] = v1 ? iv : 0.0f;
     if (fl2 < NF) {
-      pre[fl2 * 36] = v2 ? (double)rv2 : 0.0;
-      pim[fl2 * 36] = v2 ? (double)iv2 : 0.0;
+      pre[fl2 * 36] = v2 ? rv2 : 0.0f;
+      pim[fl2 * 36] = v2 ? iv2 : 0.0f;
     }
   }
 }
 
-// Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums in double, k ascending, zero basis
-// entries skipped, then the window; `out` is the frame row's band slice.  The zero entries are
+// Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums (fp32 FMAs), k ascending, zero
+// basis entries skipped, then the window; `out` is the frame row's band slice.  The zero entries are
 // known in advance: the sine basis is exactly zero at k = 0 and at n = 0 (sin 0) and nowhere
 // else, the cosine basis nowhere (cos of a nonzero multiple of pi / 8 rounds to a nonzero float:
 // cos(pi / 2) in double is 6.1e-17); the host checks both when it builds the tables.
 template <int N0>
-__device__ __forceinline__ void basis_half(const double (&rv)[9], const double (&iv)[9], float *out) {
-  double er[8], ei[8];
+__device__ __forceinline__ void basis_half(const float (&rv)[9], const float (&iv)[9], float *out) {
+  float er[8], ei[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0;
+  for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0f;
 #pragma unroll
   for (int k = 0; k < 9; ++k) {
-    const double r = rv[k], i = iv[k];
+    const float r = rv[k], i = iv[k];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      er[j] = __fma_rn(c_bcd[k * 16 + N0 + j], r, er[j]);
-      if (k != 0 && N0 + j != 0) ei[j] = __fma_rn(c_bsd[k * 16 + N0 + j], i, ei[j]);
+      er[j] = __fmaf_rn(c_bc[k * 16 + N0 + j], r, er[j]);
+      if (k != 0 && N0 + j != 0) ei[j] = __fmaf_rn(c_bs[k * 16 + N0 + j], i, ei[j]);
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) out[N0 + j] = __fmul_rn(__fadd_rn((float)er[j], (float)ei[j]), c_win[N0 + j]);
+  for (int j = 0; j < 8; ++j) out[N0 + j] = __fmul_rn(__fadd_rn(er[j], ei[j]), c_win[N0 + j]);
 }
 
-__global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a) {
+__global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a) {
   extern __shared__ __align__(16) unsigned char tail_smem[];
   TailSmem &S = *reinterpret_cast<TailSmem *>(tail_smem);
   auto &re = S.re;
@@ -186,19 +192,17 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
     const int flo = (int)flo_l, fhi = (int)fhi_l;   // valid frames [flo, fhi) of [0, NF)
     const long long cst = a.st_c;
     const float *pc = post + (long long)(b * 18 + k) * cst;
-    double *pre = &re[0][b][k], *pim = &im[0][b][k];
+    float *pre = &re[0][b][k], *pim = &im[0][b][k];
     // the fp32 / double choice is per request: one code path per CTA, not a branch per bin
     if (f32) bins_loop<true>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
     else bins_loop<false>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
   }
   __syncthreads();
-  // ---- 1b. per (frame, band, half of the 16 output bins): the 9 -> 16 basis sums in double,
-  // then the window.  A thread loads its frame's nine re / im values once and keeps 16
-  // independent chains (8 bins x re, im); items are grouped so that the 32 threads of a warp
-  // share the half, which makes every basis constant (and every zero skip) uniform across the
-  // warp.  Zero basis entries are skipped, as in the reference einsum, and each bin sums k in
-  // ascending order.  Each product of two fp32 values (24-bit significands) is exact in double,
-  // so one fused multiply-add rounds exactly where the reference's multiply-then-add does.
+  // ---- 1b. per (frame, band, half of the 16 output bins): the 9 -> 16 basis sums, then the
+  // window.  A thread loads its frame's nine re / im values once and keeps 16 independent chains
+  // (8 bins x re, im); items are grouped so that the 32 threads of a warp share the half, which
+  // makes every basis constant (and every zero skip) uniform across the warp.  Zero basis
+  // entries are skipped, as in the reference einsum, and each bin sums k in ascending order.
   {
     const int nfb = NF * 4, span = (nfb + 31) & ~31;   // (frame, band) items per half, padded
     for (int it = threadIdx.x; it < 2 * span; it += blockDim.x) {
@@ -261,10 +265,10 @@ __global__ void __launch_bounds__(kTailThreads, 3) tail_kernel(const TailArgs a)
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   float4 x0 = sm[q0], x1 = sm[q0 + 1], x2 = sm[q0 + 2], x3 = sm[q0 + 3];
   auto tap = [](float t, const float4 h, const float4 x) {
-    t = __fadd_rn(t, __fmul_rn(h.x, x.x));
-    t = __fadd_rn(t, __fmul_rn(h.y, x.y));
-    t = __fadd_rn(t, __fmul_rn(h.z, x.z));
-    return __fadd_rn(t, __fmul_rn(h.w, x.w));
+    t = __fmaf_rn(h.x, x.x, t);
+    t = __fmaf_rn(h.y, x.y, t);
+    t = __fmaf_rn(h.z, x.z, t);
+    return __fmaf_rn(h.w, x.w, t);
   };
   // (the reference skips zero inputs; adding h x 0 changes a sum only in the sign of an exact zero)
 #pragma unroll 4
@@ -311,16 +315,13 @@ static void tail_constants_init() {
       bs[k * 16 + n] = p2 / 16.0f;
     }
   }
-  double bcd[144], bsd[144];
   for (int i = 0; i < 144; ++i) {
-    bcd[i] = (double)bc[i];
-    bsd[i] = (double)bs[i];
     // the kernel skips exactly these zero entries (basis_half)
     const int k = i / 16, n = i % 16;
     if (bc[i] == 0.0f || (bs[i] == 0.0f) != (k == 0 || n == 0)) g_tail_err = 2;
   }
-  if (cudaMemcpyToSymbol(c_bcd, bcd, sizeof(bcd)) != cudaSuccess ||
-      cudaMemcpyToSymbol(c_bsd, bsd, sizeof(bsd)) != cudaSuccess ||
+  if (cudaMemcpyToSymbol(c_bc, bc, sizeof(bc)) != cudaSuccess ||
+      cudaMemcpyToSymbol(c_bs, bs, sizeof(bs)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win, win, sizeof(win)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_win2, win2, sizeof(win2)) != cudaSuccess)
     g_tail_err = 1;

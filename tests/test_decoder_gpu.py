@@ -2,7 +2,8 @@
 CPU oracle (which is bit-exact to the reference's CPU path, tests/test_oracle.py).
 
 Gates (tests/v21_reference.py:430-447, 502-505): SNDR >= 60 dB per waveform; the tail alone,
-whose arithmetic follows the reference's operation order, is held much tighter.
+whose arithmetic stays within a microunit of the reference's, is held much tighter (max_rel
+1e-5, 100 dB).
 """
 import numpy as np
 import pytest
@@ -45,7 +46,9 @@ def test_tail_matches_oracle(ctx, orc, Tp):
     ref = orc.tail(post, pq)
     y = ctx.istft_pqmf(post, pq)
     m = oracle.metrics(y, ref)
-    # only exp/sin/cos may differ (libm vs CUDA, <= 2 ulp): everything else is order-exact
+    # the kernel uses the hardware exp / sincos approximations and fp32 fused multiply-adds where
+    # the reference rounds every step (measured: max_rel <= 4.3e-7, >= 132 dB at these sizes);
+    # the gate leaves a 20x margin on the relative error and 30 dB on the SNDR
     assert m["max_rel"] <= 1e-5 and m["sndr_db"] >= 100, m
 
 
