@@ -94,6 +94,8 @@ def parse():
                     help="print the per-layer table of one decode instead of the bench line")
     ap.add_argument("--no-stream", action="store_true",
                     help="skip the config-5 sub-block of the batch workload's line")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the configs 1-3 block (GPU entry points beside the CPU path)")
     ap.add_argument("--no-distinct", action="store_true",
                     help="skip the distinct-batches e2e figure")
     ap.add_argument("--mma-rate", action="store_true",
@@ -416,6 +418,86 @@ def cpu_baseline_block(T, zs, w):
     return {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": kind,
             "cpu_model": cpu_model(), "nproc": os.cpu_count(),
             "sample": cpu_sample_text(T, picks, 2, threads) + f"; 2 steps, {dt:.1f} s wall"}
+
+
+def configs_block(dec, local):
+    """BASELINE configs 1-3 beside the CPU path, in the same run: per config the GPU through the
+    reference-facing entry points with host buffers (config 1 pt_v21_conv, config 2
+    pt_v21_convT_epi, both with resident weights as the interpreter keeps them; config 3 one
+    request through pt_b200_decode_batch, and its device-resident decode), and the reference's
+    own CPU code (oracle/_ref when it is built, else the CPU restatement) on one host thread, as
+    the reference runs one request per thread.  Outside every timed region of the bench."""
+    import torch
+    import oracle
+    kind = "reference" if os.path.exists(oracle.LIB_REF) else "oracle"
+    cpu = oracle.CpuDecoder(kind)
+    ctx = pt_b200.Context(local)
+    out = {}
+
+    def wall(fn, reps, warm=3):
+        for _ in range(warm):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    try:
+        x, wp, b = pt_b200.config1()
+        fl = 2.0 * 256 * 512 * 7 * 256
+        g = wall(lambda: ctx.conv(x, wp, b, 256, 7, 3, 1, epi0=1, a0=0.1, wtab=900, btab=901), 50)
+        c = wall(lambda: cpu.conv(x, wp, b, 256, 7, 3, 1, 1, 0, 0.1, 0.0), 2, warm=1)
+        out["config1"] = {"what": "Conv1d 512->256 k7 T=256 + LeakyReLU 0.1 (pt_v21_conv, host "
+                                  "buffers, resident weights)", "gflop": round(fl / 1e9, 5),
+                          "gpu_ms": round(g * 1e3, 4), "gpu_gflops": round(fl / g / 1e9, 1),
+                          "cpu_ms": round(c * 1e3, 2), "cpu_gflops": round(fl / c / 1e9, 2),
+                          "cpu_cores": 1, "cpu_kind": kind}
+        x, wp, b = pt_b200.config2()
+        fl = 2.0 * 512 * 256 * 16 * 256
+        g = wall(lambda: ctx.convT(x, wp, b, 256, 16, 4, 6, epi0=1, a0=0.1, wtab=902, btab=903), 50)
+        c = wall(lambda: cpu.convT(x, wp, b, 256, 16, 4, 6), 2, warm=1)
+        out["config2"] = {"what": "ConvTranspose1d 512->256 k16 s4 p6 T=256->1024 + LeakyReLU 0.1 "
+                                  "(pt_v21_convT_epi, host buffers, resident weights; the CPU leg "
+                                  "is the convT alone)", "gflop": round(fl / 1e9, 5),
+                          "gpu_ms": round(g * 1e3, 4), "gpu_gflops": round(fl / g / 1e9, 1),
+                          "cpu_ms": round(c * 1e3, 2), "cpu_gflops": round(fl / c / 1e9, 2),
+                          "cpu_cores": 1, "cpu_kind": kind}
+        w, z = pt_b200.config3(seed=2, T=226)
+        fl = pt_b200.decoder_gflop(226) * 1e9
+        audio = audio_seconds(226)
+        g = wall(lambda: dec.decode([z]), 20)
+        dev = torch.device("cuda", local)
+        zd = torch.from_numpy(z.ravel().copy()).to(dev)
+        wd = torch.empty(HOP * 226, device=dev)
+        Tz = np.array([226], np.int64)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                dec.decode_device(Tz, zd.data_ptr(), wd.data_ptr(), st.cuda_stream)
+            dec.sync(st.cuda_stream)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(20):
+                dec.decode_device(Tz, zd.data_ptr(), wd.data_ptr(), st.cuda_stream)
+            e1.record(st)
+            dec.sync(st.cuda_stream)
+        gd = e0.elapsed_time(e1) / 20 / 1e3
+        t0 = time.perf_counter()
+        cpu.decode(w, z)
+        c = time.perf_counter() - t0
+        out["config3"] = {"what": "one request, T=226 (3.616 s of audio): pt_b200_decode_batch with "
+                                  "host buffers (upload, decode, download, synchronised), and the "
+                                  "same decode device-resident", "gflop": round(fl / 1e9, 3),
+                          "gpu_ms": round(g * 1e3, 3), "gpu_audio_s_per_s": round(audio / g, 1),
+                          "gpu_device_ms": round(gd * 1e3, 3),
+                          "gpu_device_gflops": round(fl / gd / 1e9, 1),
+                          "cpu_ms": round(c * 1e3, 1), "cpu_gflops": round(fl / c / 1e9, 2),
+                          "cpu_audio_s_per_s": round(audio / c, 3), "cpu_cores": 1,
+                          "cpu_kind": kind}
+    finally:
+        ctx.close()
+    return out
 
 
 def reference_arm(args):
@@ -772,6 +854,8 @@ def main():
         out["roofline"]["note"] = "launch records of the last decode pass of a step"
     if world == 1 and not args.no_cpu_baseline and kind == "batch":
         out["cpu_baseline"] = cpu_baseline_block(T_all, zs_all, w)
+        if not args.no_configs:
+            out["configs"] = configs_block(dec, local)
     dec.close()
     emit(out)
     return 0

@@ -898,7 +898,8 @@ int pt_b200_decode_batch_async(pt_b200_decoder *d, int nreq, const int64_t *T, c
     PTB_CUDA(cudaSetDevice(d->device));
     if (async_setup(d)) return -1;
     if ((size_t)nz * 4 > d->az_bytes || (size_t)nw * 4 > d->aw_bytes) {
-      // grow both slots once nothing in flight uses them
+      // grow both slots once nothing in flight uses them, by half again so that a stream of
+      // ragged batches does not stop the pipeline at every new largest batch
       PTB_CUDA(cudaStreamSynchronize(d->h2d));
       PTB_CUDA(cudaStreamSynchronize(d->stream));
       PTB_CUDA(cudaStreamSynchronize(d->d2h));
@@ -909,12 +910,13 @@ int pt_b200_decode_batch_async(pt_b200_decoder *d, int nreq, const int64_t *T, c
         d->slot_used[k] = false;
       }
       d->az_bytes = d->aw_bytes = 0;
+      const size_t zb = (size_t)(nz + nz / 2) * 4, wb = (size_t)(nw + nw / 2) * 4;
       for (int k = 0; k < 2; ++k) {
-        PTB_CUDA(cudaMalloc(&d->az[k], (size_t)nz * 4));
-        PTB_CUDA(cudaMalloc(&d->aw[k], (size_t)nw * 4));
+        PTB_CUDA(cudaMalloc(&d->az[k], zb));
+        PTB_CUDA(cudaMalloc(&d->aw[k], wb));
       }
-      d->az_bytes = (size_t)nz * 4;
-      d->aw_bytes = (size_t)nw * 4;
+      d->az_bytes = zb;
+      d->aw_bytes = wb;
     }
     s = d->async_next;
     d->async_next ^= 1;

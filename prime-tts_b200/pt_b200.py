@@ -457,6 +457,28 @@ def load_ptk(path: str) -> DecoderWeights:
         lib().pt_b200_ptk_close(h)
 
 
+def config1(seed: int = 0):
+    """Config 1: one Conv1d 512 -> 256, k7, same padding, T = 256: x [1][512][256] ~ N(0,1), ONNX
+    weight [256][512][7] ~ N(0, 0.02^2), bias ~ N(0, 0.01^2), from one generator; returns
+    (x, packed weights, bias).  The conv is followed by LeakyReLU 0.1."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, 512, 256)).astype(np.float32)
+    W = (0.02 * rng.standard_normal((256, 512, 7))).astype(np.float32)
+    b = (0.01 * rng.standard_normal(256)).astype(np.float32)
+    return x, pack_conv(W), b
+
+
+def config2(seed: int = 1):
+    """Config 2: one ConvTranspose1d 512 -> 256, k16, s4, p6, T_in = 256 -> 1024: x ~ N(0,1),
+    ONNX weight [512][256][16] ~ N(0, 0.02^2), bias ~ N(0, 0.01^2); returns (x, packed weights,
+    bias).  The convT is followed by LeakyReLU 0.1."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, 512, 256)).astype(np.float32)
+    W = (0.02 * rng.standard_normal((512, 256, 16))).astype(np.float32)
+    b = (0.01 * rng.standard_normal(256)).astype(np.float32)
+    return x, pack_convT(W, 4), b
+
+
 def config3(seed: int = 2, T: int = 226):
     """Config 3: latent z [192][T] ~ N(0,1), then the decoder weights, from one generator."""
     rng = np.random.default_rng(seed)
