@@ -51,6 +51,14 @@ def test_tail_matches_golden(orc, gold):
     assert np.array_equal(orc.tail(tail_inputs(31, 16 * 3 + 1), pq), gold["tail_T3"])
 
 
+def test_package_config_generators_match_the_fixture_inputs():
+    """bench.py's configs 1 and 2 (pt_b200.config1 / config2) draw exactly the inputs the golden
+    fixtures were made from."""
+    for ours, fixture in ((pt_b200.config1(), cfg1_inputs()), (pt_b200.config2(), cfg2_inputs())):
+        for a, b in zip(ours, fixture):
+            assert np.array_equal(a, b)
+
+
 def test_config1_config2_match_golden(orc, gold):
     x, wp, b = cfg1_inputs()
     y1 = orc.conv(x, wp, b, 256, 7, 3, 1, 1, 0, 0.1, 0.0).ravel()
