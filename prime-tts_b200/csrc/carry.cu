@@ -560,11 +560,12 @@ int run_pass(pt_b200_carry *c, cudaStream_t st, int k, const float *z_dev, float
   {
     EpiParams e = rows_epi(t.mask_post, 80);
     e.out0 = c->POST;
+    e.frames = 1;   // POST rows hold the windowed iSTFT frames (conv_post's frames epilogue)
     if (conv(d->post, c->OUT[1], P.RP[2], -3, 1, e)) return -1;
   }
   if (P.tchunks[k] > 0 &&
       tail_run_rows(c->POST, 80, t.row0, p.tp, p.wav0, c->klo + o, c->khi + o, c->jb + o,
-                    P.tchunks[k], n, 16 * p.max_T + 1, d->pqmf, wav_dev, st))
+                    P.tchunks[k], n, 16 * p.max_T + 1, d->pqmf, wav_dev, st, 1))
     return -1;
   return 0;
 }

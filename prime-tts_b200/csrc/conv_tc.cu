@@ -101,6 +101,25 @@ int make_map_out(CUtensorMap *m, const float *base, int ld, int64_t rows) {
   return 0;
 }
 
+// Output map of conv_post's frames epilogue: [rows][ld] fp32, the frame's 64 samples in two boxes
+// of 32 floats (128 bytes) x box_rows rows, 128-byte swizzle (the staging layout).
+static int make_map_frames(CUtensorMap *m, const float *base, int ld, int64_t rows, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (encoder(&enc)) return -1;
+  PTB_REQUIRE(base && (reinterpret_cast<uintptr_t>(base) & 15) == 0 && ld % 4 == 0 && ld >= 64 &&
+                  rows > 0,
+              "pt_b200: frames map needs a 16-byte aligned base and rows of at least 64 floats");
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  PTB_REQUIRE(r == CUDA_SUCCESS, "pt_b200: frames tensor map encode failed (%d)", (int)r);
+  return 0;
+}
+
 // Output map of the upsampler epilogue: [rows][ld] fp32 viewed as (ld, 4, rows / 4), so that
 // rows 4q + p for 16 consecutive q (one phase p) are one 32-channel x 1 x 16 box.
 static int make_map_out_convt(CUtensorMap *m, const float *base, int ld, int64_t rows) {
@@ -191,7 +210,12 @@ static int launch_tn_mode(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) 
   std::memset(&to1, 0, sizeof(to1));
   if (make_map_act(&tx, L.act, L.g.cin32, L.act_rows, L.batch, kWinBox)) return -1;
   if (make_map_w(&tw, L.w, (int64_t)L.g.ntap * L.g.cin32, L.g.n_cols, kBM)) return -1;
-  if constexpr (TNTmaStore<MODE, F>::value) {
+  if constexpr (TNCfg<F>::kFrames) {
+    PTB_REQUIRE(L.g.n_cols == 128 && L.e.nstore >= 72, "pt_b200: the frames epilogue is conv_post's");
+    if (make_map_frames(&to0, L.e.out0, L.e.ldc, L.g.m_rows, 32) ||
+        make_map_frames(&to1, L.e.out0, L.e.ldc, L.g.m_rows, 16))
+      return -1;
+  } else if constexpr (TNTmaStore<MODE, F>::value) {
     if ((F & EF_OUT0) && make_map_out(&to0, L.e.out0, L.e.ldc, L.g.m_rows)) return -1;
     if ((F & EF_OUT1) && make_map_out(&to1, L.e.out1, L.e.ldc1, L.g.m_rows)) return -1;
   }
@@ -239,7 +263,7 @@ static int launch_tn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   if (e.mode == EPI_PLAIN_CONVT) return launch_tn_mode<EPI_PLAIN_CONVT, 0>(L, gerr, st);
   const int f = (e.res ? EF_RES : 0) | (e.acc_mode == 2 ? EF_ACC2 : 0) |
                 (e.acc_mode == 3 ? EF_ACC3 : 0) | (e.out0 ? EF_OUT0 : 0) |
-                (e.out1 ? EF_OUT1 : 0) | (e.refl ? EF_REFL : 0);
+                (e.out1 ? EF_OUT1 : 0) | (e.refl ? EF_REFL : 0) | (e.frames ? EF_FRAMES : 0);
   if (e.mode == EPI_ROWS_CONVT) {
     if (f == (EF_OUT0 | EF_OUT1)) return launch_tn_mode<EPI_ROWS_CONVT, EF_OUT0 | EF_OUT1>(L, gerr, st);
     return launch_tn_mode<EPI_ROWS_CONVT, EF_GENERIC>(L, gerr, st);
@@ -251,13 +275,16 @@ static int launch_tn(const ConvLaunch &L, uint32_t *gerr, cudaStream_t st) {
   switch (f) {
     case EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_OUT1>(L, gerr, st);
     case EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_OUT0>(L, gerr, st);
+    case EF_OUT0 | EF_FRAMES: return launch_tn_mode<EPI_ROWS, EF_OUT0 | EF_FRAMES>(L, gerr, st);
     case EF_RES | EF_OUT0 | EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_RES | EF_OUT0 | EF_OUT1>(L, gerr, st);
     case EF_RES | EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_RES | EF_OUT0>(L, gerr, st);
     case EF_RES | EF_ACC2 | EF_OUT0: return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC2 | EF_OUT0>(L, gerr, st);
     case EF_RES | EF_ACC3 | EF_OUT1: return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC3 | EF_OUT1>(L, gerr, st);
     case EF_RES | EF_ACC3 | EF_OUT1 | EF_REFL:
       return launch_tn_mode<EPI_ROWS, EF_RES | EF_ACC3 | EF_OUT1 | EF_REFL>(L, gerr, st);
-    default: return launch_tn_mode<EPI_ROWS, EF_GENERIC>(L, gerr, st);
+    default:
+      PTB_REQUIRE(!e.frames, "pt_b200: the frames epilogue takes out0 alone");
+      return launch_tn_mode<EPI_ROWS, EF_GENERIC>(L, gerr, st);
   }
 }
 

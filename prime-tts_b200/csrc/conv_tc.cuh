@@ -20,6 +20,7 @@
 #include <cstdint>
 
 #include "ptx.cuh"
+#include "tail_math.cuh"
 
 namespace ptb {
 
@@ -82,12 +83,14 @@ struct EpiParams {
   float alpha1;
   int refl;                   // rows marked bit1 in mask are also written to row - 2
   int out_rows;               // convT: rows of out0 / out1 (a multiple of 4; the TMA-store view)
+  int frames;                 // conv_post only: out0 rows get the 64 windowed iSTFT frame samples
 };
 
 // Compile-time shape of a decoder epilogue (the TN kernel is instantiated per combination, so
 // each instance carries only the straight-line code it needs).
 enum EpiFlags : int {
   EF_RES = 1, EF_ACC2 = 2, EF_ACC3 = 4, EF_OUT0 = 8, EF_OUT1 = 16, EF_REFL = 32,
+  EF_FRAMES = 64,    // conv_post: the epilogue computes the tail's windowed frames (below)
   EF_GENERIC = -1,   // decide everything at run time from EpiParams
 };
 
@@ -595,18 +598,22 @@ constexpr int kTNRows = 256;    // time rows per tile (MMA N)
 #ifndef PTB_RES_EW
 #define PTB_RES_EW 12
 #endif
+// The frames instance (conv_post, 72 channels, k = 7) also keeps two windows and three stages and
+// gives the rest to its epilogue's per-part staging.
 template <int F>
 struct TNCfg {
   static constexpr bool kRes = F != EF_GENERIC && (F & EF_RES);
+  static constexpr bool kFrames = F != EF_GENERIC && (F & EF_FRAMES);
+  static constexpr bool kTwoWin = kRes || kFrames;
   static constexpr int kWinRows = kTNRows + kWinHalo;             // 320
   static constexpr int kWinBytes = kWinRows * kBK * 4;            // 40 KiB
   static constexpr int kA = kBM * kBK * 4;                        // 16 KiB weight tile
   static constexpr int kGroup = PTB_TN_GROUP;                     // weight tiles per stage
   static constexpr int kAS = kA * kGroup;                         // bytes per weight stage
   // ring of windows + weight stages: (3 windows, 2 stages) or (2, 3); residual instances (2, 3)
-  static constexpr int kWinMax = kRes ? 2 : 3;                    // barrier slots
+  static constexpr int kWinMax = kTwoWin ? 2 : 3;                 // barrier slots
   static constexpr int kStageMax = 3;
-  static constexpr int kRing = kRes ? 2 * kWinBytes + 3 * kAS
+  static constexpr int kRing = kTwoWin ? 2 * kWinBytes + 3 * kAS
                                     : (3 * kWinBytes + 2 * kAS > 2 * kWinBytes + 3 * kAS
                                            ? 3 * kWinBytes + 2 * kAS
                                            : 2 * kWinBytes + 3 * kAS);
@@ -618,11 +625,17 @@ struct TNCfg {
   // run 16 epilogue warps of one staging slot each: their epilogue is a chain of short dependent
   // steps per 16-row pass, and on the 128-channel k = 3 layers it, not the MMA, sets the pace;
   // twice the warps hide twice the latency in the same registers and shared memory.
-  static constexpr int kEpiWarps = (F == EF_OUT1 || F == EF_OUT0) ? 16 : kRes ? PTB_RES_EW : 8;
+  static constexpr int kEpiWarps =
+      (F == EF_OUT1 || F == EF_OUT0 || kFrames) ? 16 : kRes ? PTB_RES_EW : 8;
   static constexpr int kThreads = 32 * (kEpiWarps + 3);
   static constexpr int kSlots = kEpiWarps == 16 ? 1 : 2;          // staging slots per warp
   static constexpr int kStageWarp = kSlots * 16 * kBK * 4;        // slots x (16 rows x 32 channels)
-  static constexpr int kStage = kEpiWarps * kStageWarp;           // 32 KiB (48 KiB at 12 warps)
+  // frames instance: per part (4 warps, 32 rows a pass) the raw 32 x 72 conv_post tile in rows of
+  // kRawLd floats, aliased at offset 0 by the two 32-row x 128-byte frame boxes (1 KiB aligned)
+  static constexpr int kRawLd = 73;
+  static constexpr int kFrPart = 10 * 1024;
+  static_assert(32 * kRawLd * 4 <= kFrPart, "frames staging: raw tile over the part's region");
+  static constexpr int kStage = kFrames ? 4 * kFrPart : kEpiWarps * kStageWarp;   // 32 / 40 / 48 KiB
   static constexpr int kBytes = kRing + kStage + 1024 + 256;
   static_assert(kBytes <= 227 * 1024, "TN kernel shared memory over the per-CTA limit");
 };
@@ -921,6 +934,8 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
   uint32_t *tmem_slot =
       reinterpret_cast<uint32_t *>(gbase + (bar0 - base) + 8 * (2 * WSM + 5 + 2 * ASM));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  // frames instance: one barrier per part of four epilogue warps (after the TMEM slot)
+  auto pbar = [&](int p) { return bar0 + 8u * (2 * WSM + 6 + 2 * ASM + p); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = g.cin32 / kBK;
@@ -946,6 +961,8 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
       mbar_init(sempty(s), 1);
     }
     mbar_init(dbar, 1);
+    if constexpr (P::kFrames)
+      for (int p = 0; p < 4; ++p) mbar_init(pbar(p), 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1114,6 +1131,118 @@ __global__ void __launch_bounds__(TNCfg<F>::kThreads, 1)
         if (n >= kWaitLimit) atomicOr(gerr, ERR_WAIT_DRAIN);
       }
     }
+  } else if constexpr (P::kFrames) {
+    // ---------------- frames epilogue (conv_post): the tail's per-frame work on the SM that holds
+    // the frame.  A part (warps 4p .. 4p+3, one per TMEM lane quarter) owns 32-row blocks of the
+    // tile as in the rows epilogue and runs each block in four steps, its warps meeting on the
+    // part's mbarrier (bounded waits) between them:
+    //   (a) quarters 0-2 load their channels' 32 accumulator columns, add the bias and store
+    //       the 32 x 72 conv_post values row-major (rows of kRawLd floats: conflict-free);
+    //   (b) thread (row = lane, band = quarter) loads its row's 9 log-magnitudes and 9 phase
+    //       logits;
+    //   (c) it computes the band's 16 windowed frame samples (frame_band: the tail kernel's
+    //       phases 1a-1b, same operations and order) and stores them, zeros for rows outside the
+    //       tile or the mask, into two 32-row x 128-byte boxes with the 128-byte swizzle
+    //       (conflict-free 16-byte stores), aliasing the raw tile;
+    //   (d) quarter 3's lane 0 stores the boxes by TMA (a 16-row box when only 16 rows remain)
+    //       and, before the next block's step (a), waits until they have been read.
+    // Quarter 3 holds no conv_post channel, so it releases the accumulator at once; quarters 0-2
+    // release it after their last block's TMEM loads.
+    const int q = warp & 3, part = warp >> 2;
+    const uint32_t reg = stg0 + static_cast<uint32_t>(part) * P::kFrPart;
+    constexpr int RL = P::kRawLd;
+    const uint32_t pb = pbar(part);
+    uint32_t pph = 0;
+    bool ok = true;
+    auto psync = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pb);
+      ok = mbar_wait(pb, pph, abort_flag, gerr, ERR_WAIT_PART);
+      pph ^= 1u;
+      return ok;
+    };
+    const int ch = q * 32 + lane;   // this lane's conv_post channel (TMEM lane)
+    const bool chok = q < 3 && ch < 72;
+    const float bias = (chok && e.bias) ? __ldg(e.bias + ch) : 0.0f;
+    const uint32_t raw_w = reg + static_cast<uint32_t>(ch) * 4u;                  // (a): column ch
+    const uint32_t raw_r = reg + static_cast<uint32_t>(lane * RL + 18 * q) * 4u;  // (b): row lane
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+      const int ab = it & 1;
+      const TNTile tile = tn_tile(g, t, mt, tt, ntiles);
+      const int r0 = tile.r0;
+      const int nblk = (tile.nr + 31) / 32, bh = (nblk + 3) / 4;
+      const int b0 = part * bh;
+      const int nb = b0 >= nblk ? 0 : (nblk - b0 < bh ? nblk - b0 : bh);
+      const int te = r0 + tile.nr < g.m_rows ? r0 + tile.nr : g.m_rows;
+      const int rb = r0 + 32 * b0;
+      unsigned vm = 0;   // bit j: this lane's row of block j is a stored frame
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tr = rb + 32 * j + lane;
+        if (j < nb && tr < te && (__ldg(e.mask + tr) & 1u)) vm |= 1u << j;
+      }
+      if (!mbar_wait(afull(ab), (it >> 1) & 1, abort_flag, gerr, ERR_WAIT_ACC)) break;
+      tc_fence_after();
+      const uint32_t tl = tmem + ab * kTNRows + (static_cast<uint32_t>(q * 32) << 16) + 32u * b0;
+      if (q == 3 || nb == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aempty(ab));
+      }
+#pragma unroll 1
+      for (int j = 0; j < nb; ++j) {
+        const int th = rb + 32 * j;
+        if (q == 3 && lane == 0) bulk_wait_read<0>();
+        if (!psync()) break;
+        if (q < 3) {   // (a)
+          float v0[16], v1[16];
+          tmem_ld16(tl + 32u * j, v0);
+          tmem_ld16(tl + 32u * j + 16u, v1);
+          if (j == nb - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(aempty(ab));
+          }
+          if (chok) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              st_shared_f32(raw_w + static_cast<uint32_t>(i * RL * 4), v0[i] + bias);
+              st_shared_f32(raw_w + static_cast<uint32_t>((16 + i) * RL * 4), v1[i] + bias);
+            }
+          }
+        }
+        if (!psync()) break;
+        float la[9], lb[9];   // (b)
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+          la[k] = ld_shared_f32(raw_r + static_cast<uint32_t>(k * 4));
+          lb[k] = ld_shared_f32(raw_r + static_cast<uint32_t>((9 + k) * 4));
+        }
+        if (!psync()) break;
+        float w[16];   // (c)
+        frame_band(la, lb, w);
+        const bool rv = (vm >> j) & 1u;
+        const uint32_t sb =
+            reg + static_cast<uint32_t>(q >> 1) * 4096u + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t u = static_cast<uint32_t>(((q & 1) * 4 + i) ^ (lane & 7));
+          st_shared_v4(sb + u * 16u, rv ? w[4 * i] : 0.0f, rv ? w[4 * i + 1] : 0.0f,
+                       rv ? w[4 * i + 2] : 0.0f, rv ? w[4 * i + 3] : 0.0f);
+        }
+        fence_proxy_async_smem();
+        if (!psync()) break;
+        if (q == 3 && lane == 0 && th < te) {   // (d)
+          const CUtensorMap *m = te - th > 16 ? &tmO0 : &tmO1;
+          tma_store_2d(m, reg, 0, th);
+          tma_store_2d(m, reg + 4096u, 32, th);
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();   // staged stores done before the CTA's memory goes
+    __syncwarp();
   } else {
     // ---------------- epilogue warps 0 .. EW-1: lane quarter (channels) x part of the time rows
     const int q = warp & 3, part = warp >> 2;

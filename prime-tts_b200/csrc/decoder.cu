@@ -563,19 +563,28 @@ int run_decoder(pt_b200_decoder *d, cudaStream_t st, const float *z_dev, float *
     }
     lvl_in = d->OUT1;
   }
-  // subband_conv_post 128 -> 72 (N tile 80), k7 p3, over the reflection-padded rows
+  // subband_conv_post 128 -> 72 (N tile 80), k7 p3, over the reflection-padded rows.  Its
+  // epilogue computes each frame's 64 windowed iSTFT samples into POST (the tail's per-frame
+  // phases), except in a checkpoint decode, which keeps conv_post's own output and runs the
+  // whole tail after it.
   const double fpost = 16 * frames + nreq;
-  rec(d, st, LK_POST, cflops(fpost, 128, 72, 7), fpost * (128 + 80) * 4, d->post.bn);
+  const int fused = d->ck_dev ? 0 : 1;
+  rec(d, st, LK_POST, cflops(fpost, 128, 72, 7) + (fused ? 2.0 * 4 * (9 * 16 + 8 * 15 + 16) * fpost : 0.0),
+      fpost * (128 + (fused ? 64 : 80)) * 4, d->post.bn);
   {
     EpiParams e = rows_epi(p.mask_post, 80);
     e.out0 = d->POST;
+    e.frames = fused;
     if (run_conv(d, st, d->post, d->P, p.R[2], -3, 1, e, nullptr, 0, rev())) return -1;
     if (ckpt(d, st, 39, d->POST, 80, 72, p.a[2][0] - 1, 16 * p.T[0] + 1)) return -1;
   }
-  // tail: algorithmic bytes = read the 72 conv_post channels + write the waveform
-  rec(d, st, LK_TAIL, 2.0 * (4 * 9 * 16 * 2 + 4 * 16 + 4 * 63 * 16) * fpost, fpost * 72 * 4 + frames * 256 * 4);
+  // tail: algorithmic bytes = read the 72 conv_post channels (or the 64 frame samples) + write
+  // the waveform
+  rec(d, st, LK_TAIL,
+      2.0 * ((fused ? 0 : 4 * 9 * 16 * 2) + 4 * 16 + 4 * 63 * 16) * fpost,
+      fpost * (fused ? 64 : 72) * 4 + frames * 256 * 4);
   if (tail_run_rows(d->POST, 80, p.row0, p.tp, p.wav0, p.klo, p.khi, nullptr, 0, nreq,
-                    16 * p.max_T + 1, d->pqmf, wav_dev, st))
+                    16 * p.max_T + 1, d->pqmf, wav_dev, st, fused))
     return -1;
   if (d->prof) cudaEventRecord(d->ev[d->nrec], st);
   return 0;
@@ -630,6 +639,8 @@ pt_b200_decoder *pt_b200_decoder_create(int device, const pt_b200_dec_weights *w
   if (cudaMalloc(&d->pqmf, 4 * 63 * 4) != cudaSuccess ||
       cudaMemcpy(d->pqmf, w->pqmf, 4 * 63 * 4, cudaMemcpyHostToDevice) != cudaSuccess)
     return fail("pqmf");
+  // the iSTFT constants conv_post's frames epilogue and the tail read, on this device
+  if (tail_prepare()) return fail("tail constants");
   return d;
 }
 

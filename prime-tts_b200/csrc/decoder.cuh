@@ -14,7 +14,7 @@ int tail_prepare();
 int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
                   const long long *wav0, const long long *klo, const long long *khi,
                   const long long *jbase, long long chunks, int nreq, long long max_tp,
-                  const float *pqmf_dev, float *wav_dev, cudaStream_t st);
+                  const float *pqmf_dev, float *wav_dev, cudaStream_t st, int frames);
 
 namespace dec {
 

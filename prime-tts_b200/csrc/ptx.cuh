@@ -16,6 +16,7 @@ enum : uint32_t {
   ERR_WAIT_ACC = 1u << 2,    // epilogue gave up waiting for the accumulator
   ERR_WAIT_DRAIN = 1u << 3,  // teardown drain ran out
   ERR_BAD_ARGS = 1u << 4,    // a kernel rejected its launch arguments
+  ERR_WAIT_PART = 1u << 5,   // an epilogue warp gave up waiting for the other warps of its rows
 };
 
 // try_wait already suspends for a hardware-defined interval per call; 1<<24 calls is seconds.
@@ -88,6 +89,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
 
 __device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
 }
 
 // TMA tile store from this CTA's shared memory (bulk async-group completion, no multicast).

@@ -21,8 +21,10 @@
 // 148 -> 123 us per config-4 decode.
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
+#include "tail_math.cuh"
 
 namespace ptb {
 
@@ -34,7 +36,7 @@ constexpr int kTailP3 = 256;
 constexpr int kTailF = kTailW / 16 + 8;      // staged frames (chunk + halo): NF <= W/16 + 5
 constexpr int kTailM = kTailW / 4 + 20;      // staged trimmed-OLA samples per band
 
-__constant__ float c_win[16], c_win2[16];
+__constant__ float c_win[16], c_win2[16];   // declared in tail_math.cuh
 __constant__ float c_bc[144], c_bs[144];   // the inverse real-DFT basis (cosine, sine rows)
 
 // Frame rows are 68 floats (4 bands x 16 + 4 pad): the overlap-add reads 8 consecutive frames at
@@ -45,6 +47,14 @@ struct TailSmem {
   float fr[kTailF][kFrStride];                 // windowed frames, [frame][band * 16 + n]
   float4 sm[kTailM];                           // trimmed OLA, 4 bands interleaved
   float4 h[63];                                // PQMF taps, 4 bands interleaved
+  float win2[16];
+};
+// The frames variant reads windowed frames that conv_post's epilogue computed (the decoder's
+// batched paths): no spectra, the frame rows staged straight from memory.
+struct TailFrSmem {
+  float fr[kTailF][kFrStride];
+  float4 sm[kTailM];
+  float4 h[63];
   float win2[16];
 };
 
@@ -60,33 +70,6 @@ struct TailArgs {
   const float *pqmf;      // [4][63]
   float *wav;
 };
-
-// magnitude / phase of one bin: re = exp(a) * cos(pi * sin(b)), im = exp(a) * sin(pi * sin(b))
-// (the cosine and sine of the phase come from one sincos call).  F32: fp32 functions, the
-// hardware approximations for exp and for the phase's sincos; otherwise double-precision ones
-// rounded to fp32 (the reference's choice for small tensors).
-template <bool F32>
-__device__ __forceinline__ void tr_bin(float la, float lb, float &rv, float &iv) {
-  float mag, sb, c, sn;
-  if constexpr (F32) {
-    mag = __expf(la);
-    sb = sinf(lb);
-  } else {
-    mag = (float)exp((double)la);
-    sb = (float)sin((double)lb);
-  }
-  const float ph = __fmul_rn(sb, 3.1415927410125732f);
-  if constexpr (F32) {
-    __sincosf(ph, &sn, &c);
-  } else {
-    double sd, cd;
-    sincos((double)ph, &sd, &cd);
-    sn = (float)sd;
-    c = (float)cd;
-  }
-  rv = __fmul_rn(mag, c);
-  iv = __fmul_rn(mag, sn);
-}
 
 // Phase 1a loop of one thread: its bin's frames fl0, fl0 + 8, ... of [0, NF), two at a time, the
 // next two frames' loads issued before this pair's math; frames outside [flo, fhi) are zeros.
@@ -124,34 +107,14 @@ __device__ __forceinline__ void bins_loop(const float *pc, long long st_t, long 
   }
 }
 
-// Bins n0 .. n0+7 of one (frame, band): the 9 -> 16 basis sums (fp32 FMAs), k ascending, zero
-// basis entries skipped, then the window; `out` is the frame row's band slice.  The zero entries are
-// known in advance: the sine basis is exactly zero at k = 0 and at n = 0 (sin 0) and nowhere
-// else, the cosine basis nowhere (cos of a nonzero multiple of pi / 8 rounds to a nonzero float:
-// cos(pi / 2) in double is 6.1e-17); the host checks both when it builds the tables.
-template <int N0>
-__device__ __forceinline__ void basis_half(const float (&rv)[9], const float (&iv)[9], float *out) {
-  float er[8], ei[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) er[j] = ei[j] = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 9; ++k) {
-    const float r = rv[k], i = iv[k];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      er[j] = __fmaf_rn(c_bc[k * 16 + N0 + j], r, er[j]);
-      if (k != 0 && N0 + j != 0) ei[j] = __fmaf_rn(c_bs[k * 16 + N0 + j], i, ei[j]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) out[N0 + j] = __fmul_rn(__fadd_rn(er[j], ei[j]), c_win[N0 + j]);
-}
-
-__global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a) {
+// FR = false: `post` holds conv_post's 72 channels per frame and the kernel runs phases 1-3.
+// FR = true: `post` holds each frame's 64 windowed samples ([band * 16 + n], conv_post's frames
+// epilogue, the same arithmetic as phases 1a-1b) and the kernel runs phases 2-3.
+template <bool FR>
+__global__ void __launch_bounds__(FR ? kTailP3 : kTailThreads, FR ? 8 : 4) tail_kernel(const TailArgs a) {
   extern __shared__ __align__(16) unsigned char tail_smem[];
-  TailSmem &S = *reinterpret_cast<TailSmem *>(tail_smem);
-  auto &re = S.re;
-  auto &im = S.im;
+  using Smem = typename std::conditional<FR, TailFrSmem, TailSmem>::type;
+  Smem &S = *reinterpret_cast<Smem *>(tail_smem);
   auto &fr = S.fr;
   auto &sm = S.sm;
   const int req = blockIdx.y;
@@ -162,8 +125,6 @@ __global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a)
   if (Tp < 2 || j0 >= nwav || j0 >= keep_hi || j0 + kTailW <= keep_lo) return;
   const long long Ls = 4 * (Tp - 1);
   const float *post = a.post + (a.row0 ? a.row0[req] : 0) * a.st_t;
-  // the reference switches Exp/Sin/Cos to fp32 libm only for tensors of >= 4096 elements
-  const bool f32 = 36 * Tp >= 4096;
 
   float *hf = reinterpret_cast<float *>(S.h);
   for (int i = threadIdx.x; i < 4 * 63; i += blockDim.x) hf[(i % 63) * 4 + i / 63] = a.pqmf[i];
@@ -180,61 +141,65 @@ __global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a)
   const long long F0 = ((m_lo + 8) >> 2) - 3;
   const int NF = (int)(((m_hi + 8) >> 2) - F0 + 1);
 
-  // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im.  Thread t owns bin t % 36 of
-  // frames t / 36, t / 36 + 8, ...: the bin's column, band and basis row are fixed per
-  // thread, so the loop carries only pointers; two frames at a time (independent chains in
-  // flight), the next two frames' loads issued before this pair's math.  Frames outside
-  // [0, Tp) never reach the overlap-add: zeros.
-  static_assert(kTailThreads == 288, "phase 1a maps 8 frames x 36 bins onto the threads");
-  {
-    const int rb = threadIdx.x % 36, fl0 = threadIdx.x / 36, b = rb / 9, k = rb - b * 9;
-    const long long flo_l = -F0 > 0 ? -F0 : 0, fhi_l = Tp - F0 < NF ? Tp - F0 : NF;
-    const int flo = (int)flo_l, fhi = (int)fhi_l;   // valid frames [flo, fhi) of [0, NF)
-    const long long cst = a.st_c;
-    const float *pc = post + (long long)(b * 18 + k) * cst;
-    float *pre = &re[0][b][k], *pim = &im[0][b][k];
-    // the fp32 / double choice is per request: one code path per CTA, not a branch per bin
-    if (f32) bins_loop<true>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
-    else bins_loop<false>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
-  }
-  __syncthreads();
-  // ---- 1b. per (frame, band, half of the 16 output bins): the 9 -> 16 basis sums, then the
-  // window.  A thread loads its frame's nine re / im values once and keeps 16 independent chains
-  // (8 bins x re, im); items are grouped so that the 32 threads of a warp share the half, which
-  // makes every basis constant (and every zero skip) uniform across the warp.  Zero basis
-  // entries are skipped, as in the reference einsum, and each bin sums k in ascending order.
-  {
-    const int nfb = NF * 4, span = (nfb + 31) & ~31;   // (frame, band) items per half, padded
-    for (int it = threadIdx.x; it < 2 * span; it += blockDim.x) {
-      const int half = it >= span, fb = it - half * span;
-      if (fb >= nfb) continue;
-      const int fl = fb >> 2, b = fb & 3;
-      // each half as its own code path: the basis offsets become compile-time constants, so the
-      // constants are instruction operands instead of one load each
-      if (half) basis_half<8>(re[fl][b], im[fl][b], &fr[fl][b * 16]);
-      else basis_half<0>(re[fl][b], im[fl][b], &fr[fl][b * 16]);
+  if constexpr (FR) {
+    // ---- 1. the windowed frames F0 + fl in [0, Tp) that the overlap-add reads, 16 float4 a row
+    for (int i = threadIdx.x; i < NF * 16; i += blockDim.x) {
+      const int fl = i >> 4, c4 = i & 15;
+      const long long qq = F0 + fl;
+      if (qq >= 0 && qq < Tp)
+        *reinterpret_cast<float4 *>(&fr[fl][4 * c4]) =
+            __ldg(reinterpret_cast<const float4 *>(post + qq * a.st_t) + c4);
     }
+    __syncthreads();
+  } else {
+    // ---- 1a. per (frame, band, bin): magnitude / phase -> re, im.  Thread t owns bin t % 36 of
+    // frames t / 36, t / 36 + 8, ...: the bin's column, band and basis row are fixed per
+    // thread, so the loop carries only pointers; two frames at a time (independent chains in
+    // flight), the next two frames' loads issued before this pair's math.  Frames outside
+    // [0, Tp) never reach the overlap-add: zeros.
+    static_assert(kTailThreads == 288, "phase 1a maps 8 frames x 36 bins onto the threads");
+    {
+      const int rb = threadIdx.x % 36, fl0 = threadIdx.x / 36, b = rb / 9, k = rb - b * 9;
+      const long long flo_l = -F0 > 0 ? -F0 : 0, fhi_l = Tp - F0 < NF ? Tp - F0 : NF;
+      const int flo = (int)flo_l, fhi = (int)fhi_l;   // valid frames [flo, fhi) of [0, NF)
+      const long long cst = a.st_c;
+      const float *pc = post + (long long)(b * 18 + k) * cst;
+      float *pre = &S.re[0][b][k], *pim = &S.im[0][b][k];
+      // the fp32 / double choice is per request: one code path per CTA, not a branch per bin;
+      // the reference switches Exp/Sin/Cos to fp32 libm only for tensors of >= 4096 elements
+      if (36 * Tp >= 4096) bins_loop<true>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
+      else bins_loop<false>(pc, a.st_t, cst, F0, NF, flo, fhi, fl0, pre, pim);
+    }
+    __syncthreads();
+    // ---- 1b. per (frame, band): the 9 -> 16 basis sums and the window (basis_sym: a thread loads
+    // its frame's nine re / im values once and keeps 18 independent chains; the basis constants
+    // are instruction operands).  Zero basis entries are skipped, as in the reference einsum,
+    // and each bin sums k in ascending order.
+    for (int it = threadIdx.x; it < NF * 4; it += blockDim.x) {
+      const int fl = it >> 2, b = it & 3;
+      basis_sym(S.re[fl][b], S.im[fl][b], &fr[fl][b * 16]);
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   // ---- 2. overlap-add / window-sum envelope, trimmed [8:-8]; frames outside [0, Tp) are absent.
   // sm[i] holds sample m_lo_raw + i; samples outside the signal (and the spare entries) are zero,
   // so phase 3 reads its whole window without bounds tests.
+  // (request-relative indices fit 32 bits: the launchers cap the frame count)
+  const int mlr = (int)m_lo_raw, mlo = (int)m_lo, mhi = (int)m_hi, f0 = (int)F0, tp = (int)Tp;
   for (int ml = threadIdx.x; ml < kTailM; ml += blockDim.x) {
-    const long long m = m_lo_raw + ml;
-    if (m < m_lo || m > m_hi) {
+    const int m = mlr + ml;
+    if (m < mlo || m > mhi) {
       sm[ml] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       continue;
     }
-    const long long p = m + 8;
-    const long long q = p >> 2;
-    const int r = (int)(p & 3);
+    const int q = (m + 8) >> 2, r = (m + 8) & 3;
     float ola[4] = {0.0f, 0.0f, 0.0f, 0.0f}, env = 0.0f;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      const long long qq = q - t;
-      if (qq >= 0 && qq < Tp) {
-        const int fl = (int)(qq - F0);
+      const int qq = q - t;
+      if (qq >= 0 && qq < tp) {
+        const int fl = qq - f0;
 #pragma unroll
         for (int b = 0; b < 4; ++b) ola[b] = __fadd_rn(ola[b], fr[fl][b * 16 + r + 4 * t]);
         env = __fadd_rn(env, S.win2[r + 4 * t]);
@@ -259,7 +224,7 @@ __global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a)
   static_assert(kTailW == 16 * kTailP3 / 4, "phase 3 gives each of its threads four outputs");
   if (threadIdx.x >= kTailP3) return;
   const int p = threadIdx.x & 3, g = threadIdx.x >> 2;
-  const int k0 = (31 - p) & 3, ntap = (63 - k0 + 3) >> 2;
+  const int k0 = (31 - p) & 3;   // 16 taps k0 + 4s, 15 for k0 = 3 (phase 0)
   // j0 is a multiple of 4, so j + k0 - 31 is: the shift divides exactly
   const int q0 = (int)(((j0 + 16 * g + p + k0 - 31) >> 2) - m_lo_raw);
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -271,8 +236,10 @@ __global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a)
     return __fmaf_rn(h.w, x.w, t);
   };
   // (the reference skips zero inputs; adding h x 0 changes a sum only in the sign of an exact zero)
-#pragma unroll 4
-  for (int s = 0; s < ntap; ++s) {
+  // Fully unrolled, so the sliding window lives in renamed registers.
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    if (s == 15 && k0 == 3) break;
     const float4 h4 = S.h[k0 + 4 * s];
     acc[0] = tap(acc[0], h4, x0);
     acc[1] = tap(acc[1], h4, x1);
@@ -281,7 +248,7 @@ __global__ void __launch_bounds__(kTailThreads, 4) tail_kernel(const TailArgs a)
     x0 = x1;
     x1 = x2;
     x2 = x3;
-    x3 = sm[q0 + s + 4];
+    if (s < 15) x3 = sm[q0 + s + 4];
   }
 #pragma unroll
   for (int v = 0; v < 4; ++v) {
@@ -316,9 +283,12 @@ static void tail_constants_init() {
     }
   }
   for (int i = 0; i < 144; ++i) {
-    // the kernel skips exactly these zero entries (basis_half)
+    // the kernels skip exactly these zero entries and mirror columns n and 16 - n (basis_sym)
     const int k = i / 16, n = i % 16;
     if (bc[i] == 0.0f || (bs[i] == 0.0f) != (k == 0 || n == 0)) g_tail_err = 2;
+    if (n > 8 && (std::fabs(bc[i] - bc[k * 16 + 16 - n]) > 1e-15f ||
+                  std::fabs(bs[i] + bs[k * 16 + 16 - n]) > 1e-15f))
+      g_tail_err = 2;
   }
   if (cudaMemcpyToSymbol(c_bc, bc, sizeof(bc)) != cudaSuccess ||
       cudaMemcpyToSymbol(c_bs, bs, sizeof(bs)) != cudaSuccess ||
@@ -338,10 +308,13 @@ static int tail_ready() {
   if (!done[dev]) {
     g_tail_err = 0;
     tail_constants_init();
-    PTB_REQUIRE(g_tail_err != 2, "pt_b200: iSTFT basis zeros differ from the kernel's assumption");
+    PTB_REQUIRE(g_tail_err != 2,
+                "pt_b200: iSTFT basis zeros or mirror symmetry differ from the kernels' assumption");
     PTB_REQUIRE(!g_tail_err, "pt_b200: tail constant upload failed");
-    PTB_CUDA(cudaFuncSetAttribute(tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PTB_CUDA(cudaFuncSetAttribute(tail_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sizeof(TailSmem)));
+    PTB_CUDA(cudaFuncSetAttribute(tail_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(TailFrSmem)));
     done[dev] = true;
   }
   return 0;
@@ -359,11 +332,12 @@ int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wa
   a.st_t = 1;
   a.st_c = Tp;
   a.tp1 = Tp;
+  PTB_REQUIRE(Tp >= 1 && Tp < (1LL << 26), "pt_b200: tail frame count %lld out of range", (long long)Tp);
   a.pqmf = pqmf_dev;
   a.wav = wav_dev;
   const long long nwav = 16 * (Tp - 1);
   dim3 grid((unsigned)((nwav + kTailW - 1) / kTailW), 1);
-  tail_kernel<<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
+  tail_kernel<false><<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;
@@ -372,10 +346,12 @@ int tail_run(const float *post_dev, int64_t Tp, const float *pqmf_dev, float *wa
 // batched requests, channels-last post rows (ld = row stride); per-request tables on the device,
 // each request writing only its kept samples.  `chunks` CTAs of kTailW samples per request start
 // at sample jbase[r] (all of a request's samples from 0 when jbase is null and chunks is 0).
+// frames = 0: the rows hold conv_post's 72 channels; 1: each row's 64 windowed frame samples
+// (conv_post's frames epilogue), and only the overlap-add and the PQMF run here.
 int tail_run_rows(const float *post_dev, long long ld, const long long *row0, const long long *tp,
                   const long long *wav0, const long long *klo, const long long *khi,
                   const long long *jbase, long long chunks, int nreq, long long max_tp,
-                  const float *pqmf_dev, float *wav_dev, cudaStream_t st) {
+                  const float *pqmf_dev, float *wav_dev, cudaStream_t st, int frames) {
   if (tail_ready()) return -1;
   TailArgs a{};
   a.post = post_dev;
@@ -389,10 +365,17 @@ int tail_run_rows(const float *post_dev, long long ld, const long long *row0, co
   a.jbase = jbase;
   a.pqmf = pqmf_dev;
   a.wav = wav_dev;
+  PTB_REQUIRE(max_tp < (1LL << 26), "pt_b200: tail frame count %lld out of range", max_tp);
   const long long nwav = 16 * (max_tp - 1);
   if (chunks <= 0) chunks = (nwav + kTailW - 1) / kTailW;
   dim3 grid((unsigned)chunks, (unsigned)nreq);
-  tail_kernel<<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
+  if (frames) {
+    PTB_REQUIRE(ld % 4 == 0 && (reinterpret_cast<uintptr_t>(post_dev) & 15) == 0,
+                "pt_b200: frame rows need 16-byte alignment");
+    tail_kernel<true><<<grid, kTailP3, sizeof(TailFrSmem), st>>>(a);
+  } else {
+    tail_kernel<false><<<grid, kTailThreads, sizeof(TailSmem), st>>>(a);
+  }
   PTB_CUDA(cudaGetLastError());
   count_launch();
   return 0;

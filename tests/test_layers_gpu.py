@@ -87,7 +87,10 @@ def dec(cfg3):
 
 
 def test_checkpoint_decode_equals_the_batched_decode(dec, cfg3):
-    """The checkpointing decode runs the same launches: its waveform is the normal decode's."""
+    """The checkpointing decode keeps conv_post's own output and runs the whole tail kernel after
+    it; the batched decode computes the windowed iSTFT frames in conv_post's epilogue (the same
+    operations in the same order) and runs only the overlap-add and the PQMF after it.  The
+    waveforms agree bit for bit (T = 40: the fp32 functions on both paths)."""
     w, z = cfg3
     _, wav = dec.checkpoints(z[:, :40].copy())
     (ref,) = dec.decode([z[:, :40].copy()])
