@@ -193,12 +193,12 @@ int ptb::dec::build_layout(Plan &p, cudaStream_t st, int nreq, const pt_b200_win
     tot += al(sz[k]);
   }
   if (tot > p.table_cap) {
-    // grow with headroom, so that later plans of similar batches reuse the buffers
+    // grow with headroom (half again), so that later plans of similar batches reuse the buffers
     if (p.table_block) cudaFree(p.table_block);
     if (p.host_stage) cudaFreeHost(p.host_stage);
     p.table_block = p.host_stage = nullptr;
     p.table_cap = 0;
-    const size_t cap = al(tot + tot / 4);
+    const size_t cap = al(tot + tot / 2);
     PTB_CUDA(cudaMalloc(&p.table_block, cap));
     PTB_CUDA(cudaMallocHost(&p.host_stage, cap));
     p.table_cap = cap;
@@ -324,12 +324,28 @@ int build_plan(pt_b200_decoder *d, cudaStream_t st, int nreq, const pt_b200_wind
         next.host_stage = old.host_stage;
         next.table_cap = old.table_cap;
         next.used = old.used;
+      } else if (!d->free_tabs.empty()) {
+        Plan t = std::move(d->free_tabs.back());
+        d->free_tabs.pop_back();
+        next.table_block = t.table_block;
+        next.host_stage = t.host_stage;
+        next.table_cap = t.table_cap;
       }
       if (!next.used) PTB_CUDA(cudaEventCreateWithFlags(&next.used, cudaEventDisableTiming));
       next.id = ++d->plan_id;
       if (build_layout(next, st, nreq, w)) {
         free_plan(next);
         return -1;
+      }
+      if (next.id == 1) {
+        // the first plan: the buffers of the plans that can be cached beside it, at its size
+        for (int k = 0; k < pt_b200_decoder::kSparePlans; ++k) {
+          d->free_tabs.emplace_back();
+          Plan &t = d->free_tabs.back();
+          PTB_CUDA(cudaMalloc(&t.table_block, next.table_cap));
+          PTB_CUDA(cudaMallocHost(&t.host_stage, next.table_cap));
+          t.table_cap = next.table_cap;
+        }
       }
     }
     if (d->have_plan) d->spare.insert(d->spare.begin(), std::move(d->plan));
@@ -666,6 +682,7 @@ void pt_b200_decoder_destroy(pt_b200_decoder *d) {
   if (d->act) cudaFree(d->act);
   free_plan(d->plan);
   for (auto &p : d->spare) free_plan(p);
+  for (auto &p : d->free_tabs) free_plan(p);
   if (d->zbuf) cudaFree(d->zbuf);
   if (d->wavbuf) cudaFree(d->wavbuf);
   if (d->gerr) cudaFree(d->gerr);

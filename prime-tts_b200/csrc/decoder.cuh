@@ -113,6 +113,10 @@ struct pt_b200_decoder {
   // least recently used plan's buffers instead of allocating
   static constexpr int kSparePlans = 4;
   std::vector<ptb::dec::Plan> spare;
+  // table buffers (device block + pinned staging) made beside the first plan's, one for each plan
+  // that can be cached, so that the first new batches after it allocate nothing (pinned
+  // allocations take milliseconds, more on a loaded host)
+  std::vector<ptb::dec::Plan> free_tabs;
   uint64_t act_plan = ~0ull;    // plan whose gap rows are zero in the activation buffers
   cudaEvent_t done = nullptr;   // recorded after every decode: plan changes wait for it
   uint64_t plan_id = 0;         // bumped whenever the plan (tables, buffers) changes
